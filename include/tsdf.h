@@ -1,0 +1,141 @@
+/*
+ * tsdf.h — C ABI of the B200 sphere tracer over .gmdag signed-distance DAGs.
+ *
+ * Library: navi_b200/_lib/libnavi_tsdf.so (sm_100a).  Every function returns
+ * TSDF_OK (0) or a negative tsdf_status; the text of the last error on the
+ * calling thread is returned by tsdf_last_error().  No function frees memory
+ * it did not allocate.  Device pointers are plain CUDA device addresses;
+ * `stream` is a cudaStream_t (NULL = legacy default stream).  All cast calls
+ * are asynchronous on `stream` and never synchronise the host.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   projects/torch-sdf/cpp_src/bindings.cpp:43-110   cast_rays_forward
+ *   projects/torch-sdf/cpp_src/kernel.cu:311-326     launch_sphere_trace_kernel
+ *   projects/torch-sdf/cpp_src/kernel.cuh:7-11       compile-time constants
+ *   projects/environment/src/navi_environment/backends/sdfdag_backend.py:1296-1312
+ *                                                     yaw-rotated fan + origin broadcast
+ *   projects/environment/src/navi_environment/backends/sdfdag_backend.py:1896-1900
+ *                                                     DAG device upload
+ */
+#ifndef NAVI_B200_TSDF_H
+#define NAVI_B200_TSDF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TSDF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TSDF_API __attribute__((visibility("default")))
+#else
+#define TSDF_API
+#endif
+
+typedef enum tsdf_status {
+    TSDF_OK = 0,
+    TSDF_ERR_INVALID = -1,     /* bad argument (null pointer, size, range) */
+    TSDF_ERR_LAYOUT = -2,      /* DAG words that cannot be traversed */
+    TSDF_ERR_CUDA = -3,        /* a CUDA runtime call failed */
+    TSDF_ERR_NO_MEMORY = -4,   /* host or device allocation failed */
+    TSDF_ERR_UNSUPPORTED = -5  /* device is not sm_100 */
+} tsdf_status;
+
+/* Reference constants (kernel.cuh:7-11, kernel.cu:9). */
+#define TSDF_DEFAULT_HIT_EPSILON 0.01f
+#define TSDF_OUTSIDE_DOMAIN_DISTANCE 1000.0f
+#define TSDF_DIRECTION_NORM_EPSILON 1e-4f
+#define TSDF_PREFIX_DEPTH 4
+
+/* Opaque device node pool built from .gmdag words (one device). */
+typedef struct tsdf_pool tsdf_pool;
+/* Opaque device table of scenes (pools + bounds + hit epsilon) for fan casts. */
+typedef struct tsdf_scenes tsdf_scenes;
+
+typedef struct tsdf_pool_stats {
+    uint64_t source_words;   /* words in the .gmdag payload */
+    uint64_t records;        /* internal nodes reachable from word 0 (32-byte records) */
+    uint64_t ext_leaves;     /* leaves with semantic >= 0x7FFF, stored out of line */
+    uint64_t device_bytes;   /* bytes of device memory held by the pool */
+    uint32_t root_slot;      /* encoded root (record 0, or a leaf) */
+    uint32_t bfs_levels;     /* BFS levels of the record graph */
+    int32_t device;          /* CUDA ordinal */
+    int32_t reserved;
+} tsdf_pool_stats;
+
+/* Per-actor pose for fan casts: 32 bytes, 16-byte aligned.  cos/sin are
+ * supplied by the caller (the reference computes them with torch.cos/sin on
+ * the device, sdfdag_backend.py:1301-1302) so the directions match it bit
+ * for bit. */
+typedef struct tsdf_pose {
+    float ox, oy, oz;
+    float cos_yaw;
+    float sin_yaw;
+    float cos_pitch;
+    float sin_pitch;
+    int32_t scene;           /* index into the tsdf_scenes table */
+} tsdf_pose;
+
+TSDF_API int tsdf_version(void);
+TSDF_API const char* tsdf_last_error(void);
+
+/* Build a node pool on `device` from .gmdag words in host memory.  Replaces
+ * the int64 DAG upload (sdfdag_backend.py:1896-1900); the words are re-packed
+ * into 32-byte records (8 child slots, one per octant).  flags: reserved, 0. */
+TSDF_API int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, uint32_t flags,
+                     tsdf_pool** out_pool);
+
+/* Same, from words already in device memory (the dag_tensor argument of
+ * torch_sdf.cast_rays).  Copies the words to the host on `stream` and waits
+ * for that copy. */
+TSDF_API int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words, int device,
+                                 uint32_t flags, void* stream, tsdf_pool** out_pool);
+
+TSDF_API int tsdf_pool_destroy(tsdf_pool* pool);
+TSDF_API int tsdf_pool_stats_get(const tsdf_pool* pool, tsdf_pool_stats* out);
+
+/* Device bytes of scratch that tsdf_cast / tsdf_cast_fan need in `workspace`
+ * (a work counter); the caller allocates it, on the device of the pool. */
+TSDF_API uint64_t tsdf_workspace_bytes(void);
+
+/* Explicit-ray cast: the semantics of sphere_trace_kernel (kernel.cu:203-309)
+ * for rays [n_rays][3] origins / dirs (f32, device), writing distance (f32),
+ * semantic (i32, 0 on miss) and, if out_steps is not NULL, the number of
+ * march iterations (i32).  Replaces launch_sphere_trace_kernel
+ * (kernel.cu:311-326) and the launch in cast_rays_forward (bindings.cpp:91-109).
+ * hit_epsilon = TSDF_DEFAULT_HIT_EPSILON reproduces the reference exactly. */
+TSDF_API int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, int64_t n_rays,
+              float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
+              float max_distance, const float bbox_min[3], const float bbox_max[3],
+              float hit_epsilon, void* workspace, void* stream);
+
+/* Scene table for fan casts: n pools with their bounds ([n][3] each, host)
+ * and hit epsilons ([n], host). */
+TSDF_API int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_min,
+                       const float* bbox_max, const float* hit_epsilon, tsdf_scenes** out);
+TSDF_API int tsdf_scenes_destroy(tsdf_scenes* scenes);
+
+/* Fused fan cast: ray (a, r) starts at pose a's origin with the local fan
+ * direction fan_dirs[r] (device, [rays_per_actor][3] f32), pitched about the
+ * local x axis when use_pitch != 0, then yaw-rotated as
+ * sdfdag_backend.py:1303-1310 does, and is traced in scene poses[a].scene.
+ * Outputs are [n_actors * rays_per_actor], actor-major. */
+TSDF_API int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
+                  const float* fan_dirs, int64_t rays_per_actor, int use_pitch,
+                  float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
+                  float max_distance, void* workspace, void* stream);
+
+/* Tuning knobs (process-wide): "smem_records" (records staged in shared
+ * memory per block, default 1024), "chunk" (rays a warp claims at once,
+ * default 32), "blocks_per_sm" (0 = occupancy maximum).  Returns the old value
+ * through *old_value when not NULL. */
+TSDF_API int tsdf_set_option(const char* key, int64_t value, int64_t* old_value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NAVI_B200_TSDF_H */

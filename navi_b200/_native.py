@@ -1,0 +1,118 @@
+"""ctypes bindings of the in-tree native libraries.
+
+The product path has no fallback: when libnavi_tsdf.so is missing or cannot be
+loaded, every call that needs it raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_DIR = Path(__file__).resolve().parent / "_lib"
+TSDF_PATH = LIB_DIR / "libnavi_tsdf.so"
+GMDAG_PATH = LIB_DIR / "libnavi_gmdag.so"
+
+_lock = threading.Lock()
+_tsdf: ctypes.CDLL | None = None
+_gmdag: ctypes.CDLL | None = None
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_int64 = ctypes.c_int64
+c_uint64 = ctypes.c_uint64
+c_uint32 = ctypes.c_uint32
+c_float = ctypes.c_float
+c_char_p = ctypes.c_char_p
+
+
+class PoolStats(ctypes.Structure):
+    _fields_ = [
+        ("source_words", c_uint64),
+        ("records", c_uint64),
+        ("ext_leaves", c_uint64),
+        ("device_bytes", c_uint64),
+        ("root_slot", c_uint32),
+        ("bfs_levels", c_uint32),
+        ("device", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+# name -> (restype, argtypes); mirrors include/tsdf.h
+TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "tsdf_version": (c_int, []),
+    "tsdf_last_error": (c_char_p, []),
+    "tsdf_pool_create": (c_int, [c_void_p, c_uint64, c_int, c_uint32, ctypes.POINTER(c_void_p)]),
+    "tsdf_pool_create_from_device": (c_int, [c_void_p, c_uint64, c_int, c_uint32, c_void_p, ctypes.POINTER(c_void_p)]),
+    "tsdf_pool_destroy": (c_int, [c_void_p]),
+    "tsdf_pool_stats_get": (c_int, [c_void_p, ctypes.POINTER(PoolStats)]),
+    "tsdf_workspace_bytes": (c_uint64, []),
+    "tsdf_cast": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                          c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p, c_void_p]),
+    "tsdf_scenes_create": (c_int, [ctypes.POINTER(c_void_p), c_int, ctypes.POINTER(c_float), ctypes.POINTER(c_float),
+                                   ctypes.POINTER(c_float), ctypes.POINTER(c_void_p)]),
+    "tsdf_scenes_destroy": (c_int, [c_void_p]),
+    "tsdf_cast_fan": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                              c_int, c_float, c_void_p, c_void_p]),
+    "tsdf_set_option": (c_int, [c_char_p, c_int64, ctypes.POINTER(c_int64)]),
+}
+
+GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "gmdag_last_error": (c_char_p, []),
+    "gmdag_compile_mesh": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int, ctypes.POINTER(c_void_p)]),
+    "gmdag_result_num_words": (c_uint64, [c_void_p]),
+    "gmdag_result_header": (None, [c_void_p, ctypes.POINTER(c_float), ctypes.POINTER(c_float), ctypes.POINTER(c_float)]),
+    "gmdag_result_copy_words": (None, [c_void_p, c_void_p]),
+    "gmdag_result_free": (None, [c_void_p]),
+    "gmdag_half_from_float": (ctypes.c_uint16, [c_float]),
+}
+
+
+def _bind(lib: ctypes.CDLL, sigs: dict[str, tuple[object, list[object]]]) -> None:
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def tsdf_lib() -> ctypes.CDLL:
+    """The trace library; raises RuntimeError when it is not built or cannot load."""
+    global _tsdf
+    if _tsdf is None:
+        with _lock:
+            if _tsdf is None:
+                if not TSDF_PATH.exists():
+                    raise RuntimeError(
+                        f"navi_b200 CUDA library not found at {TSDF_PATH}; run `python -m navi_b200.build`"
+                    )
+                lib = ctypes.CDLL(str(TSDF_PATH))
+                _bind(lib, TSDF_SIGNATURES)
+                _tsdf = lib
+    return _tsdf
+
+
+def gmdag_lib() -> ctypes.CDLL:
+    global _gmdag
+    if _gmdag is None:
+        with _lock:
+            if _gmdag is None:
+                if not GMDAG_PATH.exists():
+                    raise RuntimeError(
+                        f"navi_b200 scene compiler not found at {GMDAG_PATH}; run `python -m navi_b200.build`"
+                    )
+                lib = ctypes.CDLL(str(GMDAG_PATH))
+                _bind(lib, GMDAG_SIGNATURES)
+                _gmdag = lib
+    return _gmdag
+
+
+def last_error() -> str:
+    msg = tsdf_lib().tsdf_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed ({rc}): {last_error()}")

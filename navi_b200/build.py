@@ -1,0 +1,101 @@
+"""Build the native libraries in-tree (navi_b200/_lib/).
+
+    python -m navi_b200.build
+
+- libnavi_tsdf.so  : the sm_100a trace kernels and the C ABI of include/tsdf.h
+                     (nvcc, -gencode arch=compute_100a,code=sm_100a, static cudart)
+- libnavi_gmdag.so : the host scene compiler (g++, OpenMP, -ffp-contract=off so
+                     that its float arithmetic matches the reference compiler's)
+
+Both are rebuilt only when a source is newer than the library.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIB = PKG / "_lib"
+INCLUDE = ROOT / "include"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: the CUDA toolkit is required to build libnavi_tsdf.so")
+
+
+def host_cxx() -> str:
+    """A C++ compiler with OpenMP (the system g++ ships libgomp)."""
+    for cand in ("/usr/bin/g++", os.environ.get("CXX"), shutil.which("g++")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("no C++ compiler found")
+
+
+def host_cc() -> str:
+    for cand in ("/usr/bin/gcc", os.environ.get("CC"), shutil.which("gcc")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("no C compiler found")
+
+
+def _stale(target: Path, sources: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(s.stat().st_mtime > t for s in sources)
+
+
+def _run(cmd: list[str]) -> None:
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"build command failed ({proc.returncode}): {' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
+
+
+def build_tsdf(force: bool = False) -> Path:
+    out = LIB / "libnavi_tsdf.so"
+    srcs = [CSRC / "tsdf_trace.cu", CSRC / "tsdf_pool.cpp"]
+    deps = srcs + [CSRC / "tsdf_internal.h", INCLUDE / "tsdf.h"]
+    if force or _stale(out, deps):
+        LIB.mkdir(parents=True, exist_ok=True)
+        tmp = out.with_suffix(".so.tmp")
+        _run([
+            _nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+            "-Xcompiler", "-fvisibility=hidden", "-Xlinker", "--exclude-libs,ALL", "-diag-suppress", "186",
+            f"-I{INCLUDE}", *map(str, srcs), "-o", str(tmp),
+        ])
+        tmp.replace(out)
+    return out
+
+
+def build_gmdag(force: bool = False) -> Path:
+    out = LIB / "libnavi_gmdag.so"
+    src = CSRC / "gmdag_compiler.cpp"
+    if force or _stale(out, [src]):
+        LIB.mkdir(parents=True, exist_ok=True)
+        tmp = out.with_suffix(".so.tmp")
+        _run([
+            host_cxx(), "-O2", "-std=c++17", "-fPIC", "-shared", "-fopenmp",
+            "-ffp-contract=off", "-fno-fast-math", str(src), "-o", str(tmp),
+        ])
+        tmp.replace(out)
+    return out
+
+
+def build_all(force: bool = False) -> list[Path]:
+    return [build_tsdf(force), build_gmdag(force)]
+
+
+if __name__ == "__main__":
+    for p in build_all(force="--force" in sys.argv):
+        print(p)

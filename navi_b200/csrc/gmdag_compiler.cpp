@@ -1,0 +1,600 @@
+// Scene compiler: triangle mesh -> dense unsigned SDF -> octree DAG words (.gmdag payload).
+//
+// The output is defined by the reference voxel-dag compiler
+// (projects/voxel-dag/src/compiler.cpp); every stage below follows the same
+// arithmetic so that the words are identical for the same triangles:
+//   bounds and voxel size          compiler.cpp:313-329
+//   triangle seeding               compiler.cpp:453-490 (point-triangle distance :342-422,
+//                                  the region-based method of D. Eberly, Geometric Tools)
+//   8-direction fast sweeping      compiler.cpp:492-529 (Eikonal update :424-442)
+//   DAG build, dedup, root copy    compiler.cpp:579-674 (half conversion :542-560)
+//
+// What is different is how the work is scheduled:
+//   - seeding is split into z-slabs, one per thread (the update is a min, so the
+//     result does not depend on the order);
+//   - each sweep runs as a wavefront over (y, z) lines: a line depends only on its
+//     predecessors in y and z, which belong to the previous anti-diagonal, so the
+//     values are the ones the sequential z/y/x loop produces;
+//   - block minima and the uniform-block test read min/max pyramids instead of
+//     rescanning the block.  The uniform test |v - first| <= 1e-6f over a block
+//     equals the same test on the block's min and max, because rounded
+//     subtraction is monotone;
+//   - node dedup compares whole nodes, as the reference does after its hash
+//     lookup, so the node order (post-order DFS, octants 0..7) is the same.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <new>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+thread_local std::string g_err;
+
+struct CompileResult {
+    std::vector<uint64_t> words;
+    float bmin[3];
+    float bmax[3];
+    float voxel;
+    uint32_t resolution;
+};
+
+// compiler.cpp:342-422 — squared distance from p to triangle (v0, v1, v2).
+// The float expressions keep the reference's evaluation order.
+float point_triangle_dist_sq(float px, float py, float pz, const float* v0, const float* v1,
+                             const float* v2)
+{
+    const float dfx = px - v0[0], dfy = py - v0[1], dfz = pz - v0[2];
+    const float e0x = v1[0] - v0[0], e0y = v1[1] - v0[1], e0z = v1[2] - v0[2];
+    const float e1x = v2[0] - v0[0], e1y = v2[1] - v0[1], e1z = v2[2] - v0[2];
+    const float a00 = e0x * e0x + e0y * e0y + e0z * e0z;
+    const float a01 = e0x * e1x + e0y * e1y + e0z * e1z;
+    const float a11 = e1x * e1x + e1y * e1y + e1z * e1z;
+    const float b0 = -(dfx * e0x + dfy * e0y + dfz * e0z);
+    const float b1 = -(dfx * e1x + dfy * e1y + dfz * e1z);
+    const float det = std::fabs(a00 * a11 - a01 * a01);
+    float s = a01 * b1 - a11 * b0;
+    float t = a01 * b0 - a00 * b1;
+
+    auto edge_t = [&]() -> float {  // clamp along e1 from b1
+        if (b1 >= 0) return 0.0f;
+        if (-b1 >= a11) return 1.0f;
+        return -b1 / a11;
+    };
+    auto edge_s = [&]() -> float {  // clamp along e0 from b0
+        if (b0 >= 0) return 0.0f;
+        if (-b0 >= a00) return 1.0f;
+        return -b0 / a00;
+    };
+
+    if (s + t <= det) {
+        if (s < 0) {
+            if (t < 0) {
+                if (b0 < 0) {
+                    t = 0;
+                    s = (-b0 >= a00) ? 1.0f : -b0 / a00;
+                } else {
+                    s = 0;
+                    t = edge_t();
+                }
+            } else {
+                s = 0;
+                t = edge_t();
+            }
+        } else if (t < 0) {
+            t = 0;
+            s = edge_s();
+        } else {
+            const float inv = 1.0f / det;
+            s *= inv;
+            t *= inv;
+        }
+    } else {
+        if (s < 0) {
+            const float tmp0 = a01 + b0;
+            const float tmp1 = a11 + b1;
+            if (tmp1 > tmp0) {
+                const float numer = tmp1 - tmp0;
+                const float denom = a00 - 2.0f * a01 + a11;
+                s = (numer >= denom) ? 1.0f : numer / denom;
+                t = 1 - s;
+            } else {
+                s = 0;
+                if (tmp1 >= 0) t = 0;
+                else if (-b1 >= a11) t = 1;
+                else t = -b1 / a11;
+            }
+        } else if (t < 0) {
+            const float tmp0 = a01 + b1;
+            const float tmp1 = a00 + b0;
+            if (tmp1 > tmp0) {
+                const float numer = tmp1 - tmp0;
+                const float denom = a00 - 2.0f * a01 + a11;
+                t = (numer >= denom) ? 1.0f : numer / denom;
+                s = 1 - t;
+            } else {
+                t = 0;
+                if (tmp1 >= 0) s = 0;
+                else if (-b0 >= a00) s = 1;
+                else s = -b0 / a00;
+            }
+        } else {
+            const float numer = a11 + b1 - a01 - b0;
+            if (numer <= 0) {
+                s = 0;
+                t = 1;
+            } else {
+                const float denom = a00 - 2.0f * a01 + a11;
+                s = (numer >= denom) ? 1.0f : numer / denom;
+                t = 1 - s;
+            }
+        }
+    }
+    const float rx = v0[0] + s * e0x + t * e1x - px;
+    const float ry = v0[1] + s * e0y + t * e1y - py;
+    const float rz = v0[2] + s * e0z + t * e1z - pz;
+    return rx * rx + ry * ry + rz * rz;
+}
+
+// compiler.cpp:424-442 — Godunov upwind update from the three sorted neighbours.
+inline float eikonal_update(float a, float b, float c, float h)
+{
+    if (a > b) std::swap(a, b);
+    if (b > c) std::swap(b, c);
+    if (a > b) std::swap(a, b);
+    float d = a + h;
+    if (d <= b) return d;
+    d = 0.5f * (a + b + std::sqrt(2.0f * h * h - (a - b) * (a - b)));
+    if (d <= c) return d;
+    const float sum = a + b + c;
+    const float sum_sq = a * a + b * b + c * c;
+    const float disc = sum * sum - 3.0f * (sum_sq - h * h);
+    if (disc >= 0.0f) return (sum + std::sqrt(disc)) / 3.0f;
+    return d;
+}
+
+// compiler.cpp:542-560.  Truncating float->half with an unsigned exponent: a biased
+// exponent below 112 (|f| < 2^-15, zero included) wraps and encodes as infinity.
+// The reference behaves this way and the DAG words must match it.
+uint16_t half_from_float_ref(float f)
+{
+    uint32_t i;
+    std::memcpy(&i, &f, sizeof i);
+    const uint32_t s = (i >> 16) & 0x00008000u;
+    const uint32_t e = ((i >> 23) & 0x000000ffu) - (127u - 15u);
+    uint32_t m = i & 0x007fffffu;
+    if (e == 0u) {  // the reference's `e <= 0` on an unsigned value
+        m = (m | 0x00800000u) >> 1;
+        return static_cast<uint16_t>(s | (m >> 13));
+    }
+    if (e == 0xffu - (127u - 15u)) {
+        if (m == 0) return static_cast<uint16_t>(s | 0x7c00u);
+        return static_cast<uint16_t>(s | 0x7c00u | (m >> 13) | 1u);
+    }
+    if (e > 30u) return static_cast<uint16_t>(s | 0x7c00u);
+    return static_cast<uint16_t>(s | (e << 10) | (m >> 13));
+}
+
+uint64_t leaf_word(float dist, uint16_t semantic)
+{
+    return (1ull << 63) | (static_cast<uint64_t>(semantic) << 16) |
+           static_cast<uint64_t>(half_from_float_ref(dist));
+}
+
+int threads_or_default(int n_threads)
+{
+#ifdef _OPENMP
+    return n_threads > 0 ? n_threads : omp_get_max_threads();
+#else
+    (void)n_threads;
+    return 1;
+#endif
+}
+
+// ---------------------------------------------------------------- SDF stage
+
+void seed_triangles(std::vector<float>& grid, int N, const float* bmin, float dx, float dy,
+                    float dz, float h, const float* verts, const uint32_t* idx, uint64_t n_tri,
+                    int n_threads)
+{
+    const int T = threads_or_default(n_threads);
+#ifdef _OPENMP
+#pragma omp parallel num_threads(T)
+#endif
+    {
+#ifdef _OPENMP
+        const int tid = omp_get_thread_num();
+        const int nth = omp_get_num_threads();
+#else
+        const int tid = 0, nth = 1;
+#endif
+        const int z_lo = static_cast<int>(static_cast<int64_t>(N) * tid / nth);
+        const int z_hi = static_cast<int>(static_cast<int64_t>(N) * (tid + 1) / nth) - 1;
+        for (uint64_t tr = 0; tr < n_tri; ++tr) {
+            const float* v0 = &verts[static_cast<size_t>(idx[3 * tr]) * 3];
+            const float* v1 = &verts[static_cast<size_t>(idx[3 * tr + 1]) * 3];
+            const float* v2 = &verts[static_cast<size_t>(idx[3 * tr + 2]) * 3];
+            const float lo_x = std::min({v0[0], v1[0], v2[0]}) - h;
+            const float hi_x = std::max({v0[0], v1[0], v2[0]}) + h;
+            const float lo_y = std::min({v0[1], v1[1], v2[1]}) - h;
+            const float hi_y = std::max({v0[1], v1[1], v2[1]}) + h;
+            const float lo_z = std::min({v0[2], v1[2], v2[2]}) - h;
+            const float hi_z = std::max({v0[2], v1[2], v2[2]}) + h;
+            const int x0 = std::max(0, static_cast<int>((lo_x - bmin[0]) / dx));
+            const int x1 = std::min(N - 1, static_cast<int>((hi_x - bmin[0]) / dx));
+            const int y0 = std::max(0, static_cast<int>((lo_y - bmin[1]) / dy));
+            const int y1 = std::min(N - 1, static_cast<int>((hi_y - bmin[1]) / dy));
+            int zs = std::max(0, static_cast<int>((lo_z - bmin[2]) / dz));
+            int ze = std::min(N - 1, static_cast<int>((hi_z - bmin[2]) / dz));
+            zs = std::max(zs, z_lo);
+            ze = std::min(ze, z_hi);
+            for (int z = zs; z <= ze; ++z) {
+                const float pz = bmin[2] + z * dz;
+                for (int y = y0; y <= y1; ++y) {
+                    const float py = bmin[1] + y * dy;
+                    float* row = &grid[(static_cast<size_t>(z) * N + y) * N];
+                    for (int x = x0; x <= x1; ++x) {
+                        const float px = bmin[0] + x * dx;
+                        const float d = std::sqrt(point_triangle_dist_sq(px, py, pz, v0, v1, v2));
+                        if (d < row[x]) row[x] = d;
+                    }
+                }
+            }
+        }
+    }
+}
+
+void fast_sweep(std::vector<float>& grid, int N, float h, int n_threads)
+{
+    static const int kDirs[8][3] = {{1, 1, 1},  {-1, 1, 1},  {1, -1, 1},  {-1, -1, 1},
+                                    {1, 1, -1}, {-1, 1, -1}, {1, -1, -1}, {-1, -1, -1}};
+    const float kBig = std::numeric_limits<float>::max();
+    const size_t NN = static_cast<size_t>(N) * N;
+    const int T = threads_or_default(n_threads);
+    for (int sw = 0; sw < 8; ++sw) {
+        const int sx = kDirs[sw][0], sy = kDirs[sw][1], sz = kDirs[sw][2];
+        // anti-diagonal j = y' + z' in sweep coordinates; lines on one diagonal are independent
+        for (int j = 0; j <= 2 * (N - 1); ++j) {
+            const int yp_lo = std::max(0, j - (N - 1));
+            const int yp_hi = std::min(N - 1, j);
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(T) schedule(static) if (yp_hi - yp_lo > 8)
+#endif
+            for (int yp = yp_lo; yp <= yp_hi; ++yp) {
+                const int zp = j - yp;
+                const int y = sy > 0 ? yp : N - 1 - yp;
+                const int z = sz > 0 ? zp : N - 1 - zp;
+                float* row = &grid[static_cast<size_t>(z) * NN + static_cast<size_t>(y) * N];
+                const bool has_b = (y - sy >= 0 && y - sy < N);
+                const bool has_c = (z - sz >= 0 && z - sz < N);
+                const float* row_b = has_b ? row - static_cast<ptrdiff_t>(sy) * N : nullptr;
+                const float* row_c = has_c ? row - static_cast<ptrdiff_t>(sz) * static_cast<ptrdiff_t>(NN) : nullptr;
+                for (int xp = 0; xp < N; ++xp) {
+                    const int x = sx > 0 ? xp : N - 1 - xp;
+                    const float a = (x - sx >= 0 && x - sx < N) ? row[x - sx] : kBig;
+                    const float b = has_b ? row_b[x] : kBig;
+                    const float c = has_c ? row_c[x] : kBig;
+                    const float u = eikonal_update(a, b, c, h);
+                    if (u < row[x]) row[x] = u;
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- DAG stage
+
+// min/max of aligned blocks of size 2^L, L = 1..log2(N); level 0 is the grid itself.
+struct Pyramid {
+    int N = 0;
+    int levels = 0;
+    std::vector<std::vector<float>> mn, mx;
+
+    static bool is_pow2(int n) { return n > 0 && (n & (n - 1)) == 0; }
+
+    void build(const std::vector<float>& grid, int n, int n_threads)
+    {
+        N = n;
+        levels = 0;
+        while ((1 << levels) < N) ++levels;
+        mn.assign(levels + 1, {});
+        mx.assign(levels + 1, {});
+        const int T = threads_or_default(n_threads);
+        for (int L = 1; L <= levels; ++L) {
+            const int M = N >> L;
+            const int P = N >> (L - 1);
+            mn[L].resize(static_cast<size_t>(M) * M * M);
+            mx[L].resize(static_cast<size_t>(M) * M * M);
+            const float* smn = (L == 1) ? grid.data() : mn[L - 1].data();
+            const float* smx = (L == 1) ? grid.data() : mx[L - 1].data();
+            float* dmn = mn[L].data();
+            float* dmx = mx[L].data();
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(T) schedule(static)
+#endif
+            for (int z = 0; z < M; ++z) {
+                for (int y = 0; y < M; ++y) {
+                    for (int x = 0; x < M; ++x) {
+                        float lo = std::numeric_limits<float>::infinity();
+                        float hi = -std::numeric_limits<float>::infinity();
+                        for (int k = 0; k < 8; ++k) {
+                            const size_t s = (static_cast<size_t>(2 * z + ((k >> 2) & 1)) * P +
+                                              (2 * y + ((k >> 1) & 1))) * P + (2 * x + (k & 1));
+                            lo = std::min(lo, smn[s]);
+                            hi = std::max(hi, smx[s]);
+                        }
+                        const size_t d = (static_cast<size_t>(z) * M + y) * M + x;
+                        dmn[d] = lo;
+                        dmx[d] = hi;
+                    }
+                }
+            }
+        }
+    }
+};
+
+class DagBuilder {
+public:
+    DagBuilder(const std::vector<float>& grid, int N, float voxel, const Pyramid* pyr)
+        : grid_(grid), N_(N), voxel_(voxel), pyr_(pyr)
+    {
+    }
+
+    std::vector<uint64_t> run()
+    {
+        pool_.clear();
+        pool_.push_back(0);  // compiler.cpp:663 — index 0 reserved for the root copy
+        const uint32_t root = build(0, 0, 0, N_);
+        pool_[0] = pool_[root];  // compiler.cpp:671
+        return std::move(pool_);
+    }
+
+private:
+    const std::vector<float>& grid_;
+    const int N_;
+    const float voxel_;
+    const Pyramid* pyr_;
+    std::vector<uint64_t> pool_;
+    std::unordered_map<uint64_t, uint32_t> leaves_;
+    // internal nodes: hash of (mask, children) -> candidate node indices
+    std::unordered_map<uint64_t, std::vector<uint32_t>> internals_;
+
+    float at(int x, int y, int z) const
+    {
+        return grid_[(static_cast<size_t>(z) * N_ + y) * N_ + x];
+    }
+
+    int level_of(int size) const
+    {
+        int L = 0;
+        while ((1 << L) < size) ++L;
+        return L;
+    }
+
+    // compiler.cpp:563-577 (min over the block, clipped to the grid)
+    float block_min(int x, int y, int z, int size) const
+    {
+        if (pyr_ && (size & (size - 1)) == 0 && x % size == 0 && y % size == 0 &&
+            z % size == 0 && x + size <= N_ && y + size <= N_ && z + size <= N_) {
+            if (size == 1) return at(x, y, z);
+            const int L = level_of(size);
+            const int M = N_ >> L;
+            return pyr_->mn[L][(static_cast<size_t>(z / size) * M + y / size) * M + x / size];
+        }
+        float m = std::numeric_limits<float>::max();
+        for (int bz = z; bz < z + size && bz < N_; ++bz)
+            for (int by = y; by < y + size && by < N_; ++by)
+                for (int bx = x; bx < x + size && bx < N_; ++bx) m = std::min(m, at(bx, by, bz));
+        return m;
+    }
+
+    // compiler.cpp:600-613: every voxel of the block within 1e-6f of the first one
+    bool block_uniform(int x, int y, int z, int size, float first) const
+    {
+        if (pyr_ && (size & (size - 1)) == 0 && x % size == 0 && y % size == 0 &&
+            z % size == 0 && x + size <= N_ && y + size <= N_ && z + size <= N_) {
+            const int L = level_of(size);
+            const int M = N_ >> L;
+            const size_t k = (static_cast<size_t>(z / size) * M + y / size) * M + x / size;
+            const float lo = pyr_->mn[L][k], hi = pyr_->mx[L][k];
+            return !(std::fabs(hi - first) > 1e-6f) && !(std::fabs(lo - first) > 1e-6f);
+        }
+        for (int bz = z; bz < z + size && bz < N_; ++bz)
+            for (int by = y; by < y + size && by < N_; ++by)
+                for (int bx = x; bx < x + size && bx < N_; ++bx)
+                    if (std::fabs(at(bx, by, bz) - first) > 1e-6f) return false;
+        return true;
+    }
+
+    uint32_t add_leaf(uint64_t w)
+    {
+        auto it = leaves_.find(w);
+        if (it != leaves_.end()) return it->second;
+        const uint32_t p = static_cast<uint32_t>(pool_.size());
+        pool_.push_back(w);
+        leaves_.emplace(w, p);
+        return p;
+    }
+
+    static uint64_t mix(uint64_t h, uint64_t v)
+    {
+        h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+        return h;
+    }
+
+    uint32_t add_internal(uint8_t mask, const uint32_t* kids, int n)
+    {
+        uint64_t h = mask;
+        for (int i = 0; i < n; ++i) h = mix(h, kids[i]);
+        auto& bucket = internals_[h];
+        for (uint32_t cand : bucket) {
+            const uint64_t w = pool_[cand];
+            if (static_cast<uint8_t>((w >> 55) & 0xFF) != mask) continue;
+            const uint32_t base = static_cast<uint32_t>(w & 0xFFFFFFFFu);
+            bool same = true;
+            for (int i = 0; i < n && same; ++i) same = (pool_[base + i] == kids[i]);
+            if (same) return cand;
+        }
+        const uint32_t p = static_cast<uint32_t>(pool_.size());
+        pool_.push_back(0);
+        const uint32_t base = static_cast<uint32_t>(pool_.size());
+        for (int i = 0; i < n; ++i) pool_.push_back(kids[i]);
+        pool_[p] = (static_cast<uint64_t>(mask) << 55) | base;
+        bucket.push_back(p);
+        return p;
+    }
+
+    // compiler.cpp:579-659
+    uint32_t build(int x, int y, int z, int size)
+    {
+        const float two_vox = voxel_ * 2.0f;
+        if (size == 1) {
+            const float d = at(x, y, z);
+            return add_leaf(leaf_word(d, d < two_vox ? 1 : 0));
+        }
+        const float first = at(x, y, z);
+        if (block_uniform(x, y, z, size, first)) {
+            return add_leaf(leaf_word(first, first < two_vox ? 1 : 0));
+        }
+        const int half = size / 2;
+        const float octant_extent = static_cast<float>(half) * voxel_ * 1.7321f;
+        uint8_t mask = 0;
+        uint32_t kids[8];
+        int n = 0;
+        for (int i = 0; i < 8; ++i) {
+            const int ox = (i & 1) ? half : 0;
+            const int oy = (i & 2) ? half : 0;
+            const int oz = (i & 4) ? half : 0;
+            if (block_min(x + ox, y + oy, z + oz, half) > octant_extent) continue;
+            kids[n++] = build(x + ox, y + oy, z + oz, half);
+            mask |= static_cast<uint8_t>(1u << i);
+        }
+        if (mask == 0) {
+            const float m = block_min(x, y, z, size);
+            return add_leaf((1ull << 63) | static_cast<uint64_t>(half_from_float_ref(m)));
+        }
+        return add_internal(mask, kids, n);
+    }
+};
+
+// compiler.cpp:313-329
+void mesh_bounds(const float* verts, uint64_t n_verts, uint32_t res, float* bmin, float* bmax,
+                 float* voxel)
+{
+    float lo[3] = {std::numeric_limits<float>::max(), std::numeric_limits<float>::max(),
+                   std::numeric_limits<float>::max()};
+    float hi[3] = {std::numeric_limits<float>::lowest(), std::numeric_limits<float>::lowest(),
+                   std::numeric_limits<float>::lowest()};
+    for (uint64_t v = 0; v < n_verts; ++v) {
+        for (int a = 0; a < 3; ++a) {
+            const float c = verts[3 * v + a];
+            if (c < lo[a]) lo[a] = c;
+            if (c > hi[a]) hi[a] = c;
+        }
+    }
+    const float ext = std::max({hi[0] - lo[0], hi[1] - lo[1], hi[2] - lo[2]});
+    *voxel = (ext + 2.0f) / static_cast<float>(res);
+    for (int a = 0; a < 3; ++a) {
+        const float c = (hi[a] + lo[a]) / 2.0f;
+        bmin[a] = c - (ext + 2.0f) / 2.0f;
+        bmax[a] = c + (ext + 2.0f) / 2.0f;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gmdag_last_error(void) { return g_err.c_str(); }
+
+// Compile a triangle mesh.  verts: [n_verts][3] f32, idx: [n_tri][3] u32.
+// On success *out receives an opaque result; read it with gmdag_result_* and
+// release it with gmdag_result_free.  Returns 0 or a negative error code.
+int gmdag_compile_mesh(const float* verts, uint64_t n_verts, const uint32_t* idx, uint64_t n_tri,
+                       uint32_t resolution, int n_threads, void** out)
+{
+    g_err.clear();
+    if (!out) {
+        g_err = "out must not be null";
+        return -1;
+    }
+    *out = nullptr;
+    if (!verts || n_verts == 0 || !idx || n_tri == 0) {
+        g_err = "mesh must contain at least one triangle";
+        return -1;
+    }
+    if (resolution == 0 || resolution > 4096) {
+        g_err = "resolution must be in [1, 4096]";
+        return -1;
+    }
+    for (uint64_t i = 0; i < 3 * n_tri; ++i) {
+        if (idx[i] >= n_verts) {
+            g_err = "triangle index out of range";
+            return -1;
+        }
+    }
+    try {
+        auto res = std::make_unique<CompileResult>();
+        res->resolution = resolution;
+        mesh_bounds(verts, n_verts, resolution, res->bmin, res->bmax, &res->voxel);
+        const int N = static_cast<int>(resolution);
+        // compiler.cpp:446-451
+        std::vector<float> grid(static_cast<size_t>(N) * N * N, std::numeric_limits<float>::max());
+        const float dx = (res->bmax[0] - res->bmin[0]) / N;
+        const float dy = (res->bmax[1] - res->bmin[1]) / N;
+        const float dz = (res->bmax[2] - res->bmin[2]) / N;
+        const float h = std::min({dx, dy, dz});
+        seed_triangles(grid, N, res->bmin, dx, dy, dz, h, verts, idx, n_tri, n_threads);
+        fast_sweep(grid, N, h, n_threads);
+        Pyramid pyr;
+        const bool use_pyr = Pyramid::is_pow2(N) && N > 1;
+        if (use_pyr) pyr.build(grid, N, n_threads);
+        DagBuilder b(grid, N, res->voxel, use_pyr ? &pyr : nullptr);
+        res->words = b.run();
+        if (res->words.size() > 0xFFFFFFFFull) {
+            g_err = "DAG exceeds 2^32 words";
+            return -2;
+        }
+        *out = res.release();
+        return 0;
+    } catch (const std::bad_alloc&) {
+        g_err = "out of host memory while compiling";
+        return -3;
+    }
+}
+
+uint64_t gmdag_result_num_words(const void* r)
+{
+    return r ? static_cast<const CompileResult*>(r)->words.size() : 0;
+}
+
+void gmdag_result_header(const void* r, float* bmin, float* bmax, float* voxel)
+{
+    const auto* c = static_cast<const CompileResult*>(r);
+    for (int a = 0; a < 3; ++a) {
+        bmin[a] = c->bmin[a];
+        bmax[a] = c->bmax[a];
+    }
+    *voxel = c->voxel;
+}
+
+void gmdag_result_copy_words(const void* r, uint64_t* dst)
+{
+    const auto* c = static_cast<const CompileResult*>(r);
+    std::memcpy(dst, c->words.data(), c->words.size() * sizeof(uint64_t));
+}
+
+void gmdag_result_free(void* r) { delete static_cast<CompileResult*>(r); }
+
+// The reference's float->half conversion, exposed for tests.
+uint16_t gmdag_half_from_float(float f) { return half_from_float_ref(f); }
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// Internal types shared by the pool builder and the trace kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "tsdf.h"
+
+namespace tsdf {
+
+// ---- child-slot encoding of the re-packed pool -------------------------------
+// A record is one internal DAG node: 8 u32 slots indexed by octant
+// (x | y<<1 | z<<2, kernel.cu:171).  A slot holds one of:
+//   kSlotVoid                 mask bit clear: empty octant (kernel.cu:177-190)
+//   1 | sem:15 | half:16      leaf inline (semantic < 0x7FFF)
+//   01 | index:30             leaf stored out of line (semantic >= 0x7FFF)
+//   00 | record:30            internal child
+constexpr uint32_t kSlotVoid = 0xFFFFFFFFu;
+constexpr uint32_t kSlotLeafBit = 0x80000000u;
+constexpr uint32_t kSlotExtBit = 0x40000000u;
+constexpr uint32_t kSlotIndexMask = 0x3FFFFFFFu;
+constexpr uint32_t kMaxRecords = 0x3FFFFFFFu;
+
+inline uint32_t encode_leaf_inline(uint64_t word)
+{
+    const uint32_t sem = static_cast<uint32_t>((word >> 16) & 0xFFFFu);
+    return kSlotLeafBit | (sem << 16) | static_cast<uint32_t>(word & 0xFFFFu);
+}
+
+struct HostPool {
+    std::vector<uint32_t> recs;      // 8 per record
+    std::vector<uint64_t> ext;       // out-of-line leaf words
+    uint32_t root = kSlotVoid;
+    uint32_t levels = 0;
+};
+
+// Re-pack .gmdag words; returns TSDF_OK or an error with `err` set.
+int build_host_pool(const uint64_t* words, uint64_t n, HostPool& out, std::string& err);
+
+}  // namespace tsdf
+
+struct tsdf_pool {
+    int device = 0;
+    uint32_t* d_recs = nullptr;      // [records][8]
+    uint64_t* d_ext = nullptr;       // [ext leaves]
+    uint64_t records = 0;
+    uint64_t ext = 0;
+    uint64_t source_words = 0;
+    uint64_t bytes = 0;
+    uint32_t root = tsdf::kSlotVoid;
+    uint32_t levels = 0;
+};
+
+// Device view of one scene (fan casts index a table of these).
+struct TsdfSceneDev {
+    const uint32_t* recs;
+    const uint64_t* ext;
+    uint32_t root;
+    uint32_t n_recs;
+    float bmin[3];
+    float bmax[3];
+    float eps;
+    float pad_;
+};
+static_assert(sizeof(TsdfSceneDev) == 56, "scene record layout");
+
+struct tsdf_scenes {
+    int device = 0;
+    int n = 0;
+    TsdfSceneDev* d_table = nullptr;
+    std::vector<TsdfSceneDev> host;
+};
+
+namespace tsdf {
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+}  // namespace tsdf

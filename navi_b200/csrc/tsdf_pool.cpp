@@ -1,0 +1,329 @@
+// Pool builder: .gmdag words -> 32-byte octant records, plus the pool and
+// scene-table entry points of the C ABI.
+//
+// The reference traverses the raw words: per level it loads the node word and
+// then the child-pointer word (kernel.cu:137, :198).  Here every internal node
+// reachable from word 0 becomes one record of 8 u32 slots indexed directly by
+// octant, so a level costs one 4-byte load from one 32-byte sector, and a leaf
+// child is decoded from the slot without another load.  Records are numbered
+// in BFS order from the root, so the top levels are contiguous at the start of
+// the pool (they are staged in shared memory by the trace kernel).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <deque>
+#include <new>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "tsdf_internal.h"
+
+namespace tsdf {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg)
+{
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return TSDF_ERR_CUDA;
+}
+
+const char* last_error_cstr() { return g_last_error.c_str(); }
+
+int build_host_pool(const uint64_t* w, uint64_t n, HostPool& hp, std::string& err)
+{
+    if (n == 0) {
+        err = "DAG payload is empty";
+        return TSDF_ERR_LAYOUT;
+    }
+    if (n > 0xFFFFFFFFull + 1) {
+        err = "DAG payload exceeds 2^32 words";
+        return TSDF_ERR_LAYOUT;
+    }
+    std::vector<int32_t> rec_of(static_cast<size_t>(n), -1);
+    std::vector<uint32_t> rec_node;  // record -> source word index
+    std::vector<uint32_t> rec_level;
+    std::unordered_map<uint64_t, uint32_t> ext_of;
+    hp.recs.clear();
+    hp.ext.clear();
+
+    auto encode = [&](uint32_t idx, uint32_t level, uint32_t& slot) -> int {
+        const uint64_t word = w[idx];
+        if ((word >> 63) == 1) {
+            const uint32_t sem = static_cast<uint32_t>((word >> 16) & 0xFFFFu);
+            if (sem < 0x7FFFu) {
+                slot = encode_leaf_inline(word);
+                return TSDF_OK;
+            }
+            const uint64_t key = word & 0x80000000FFFFFFFFull;
+            auto it = ext_of.find(key);
+            if (it == ext_of.end()) {
+                if (hp.ext.size() >= kMaxRecords) {
+                    err = "too many out-of-line leaves";
+                    return TSDF_ERR_LAYOUT;
+                }
+                it = ext_of.emplace(key, static_cast<uint32_t>(hp.ext.size())).first;
+                hp.ext.push_back(word);
+            }
+            slot = kSlotExtBit | it->second;
+            return TSDF_OK;
+        }
+        if (rec_of[idx] < 0) {
+            if (rec_node.size() >= kMaxRecords) {
+                err = "too many internal nodes";
+                return TSDF_ERR_LAYOUT;
+            }
+            rec_of[idx] = static_cast<int32_t>(rec_node.size());
+            rec_node.push_back(idx);
+            rec_level.push_back(level);
+        }
+        slot = static_cast<uint32_t>(rec_of[idx]);
+        return TSDF_OK;
+    };
+
+    int rc = encode(0, 0, hp.root);
+    if (rc != TSDF_OK) return rc;
+    uint32_t max_level = 0;
+    for (size_t r = 0; r < rec_node.size(); ++r) {
+        const uint32_t idx = rec_node[r];
+        const uint32_t lvl = rec_level[r];
+        max_level = std::max(max_level, lvl);
+        const uint64_t word = w[idx];
+        const uint32_t mask = static_cast<uint32_t>((word >> 55) & 0xFFu);
+        const uint64_t base = word & 0xFFFFFFFFull;
+        uint32_t slots[8];
+        for (int oct = 0; oct < 8; ++oct) {
+            if ((mask & (1u << oct)) == 0) {
+                slots[oct] = kSlotVoid;
+                continue;
+            }
+            const uint64_t ci = base + static_cast<uint64_t>(__builtin_popcount(mask & ((1u << oct) - 1u)));
+            if (ci >= n) {
+                err = "Invalid gmdag DAG layout: child pointer table exceeds payload bounds for node " +
+                      std::to_string(idx);
+                return TSDF_ERR_LAYOUT;
+            }
+            const uint32_t child = static_cast<uint32_t>(w[ci]);
+            if (child >= n) {
+                err = "Invalid gmdag DAG layout: child reference out of range (" +
+                      std::to_string(child) + ") from node " + std::to_string(idx);
+                return TSDF_ERR_LAYOUT;
+            }
+            rc = encode(child, lvl + 1, slots[oct]);
+            if (rc != TSDF_OK) return rc;
+        }
+        hp.recs.insert(hp.recs.end(), slots, slots + 8);
+    }
+    hp.levels = rec_node.empty() ? 0 : max_level + 1;
+    return TSDF_OK;
+}
+
+}  // namespace tsdf
+
+using tsdf::cuda_fail;
+using tsdf::fail;
+
+extern "C" {
+
+const char* tsdf_last_error(void) { return tsdf::last_error_cstr(); }
+
+int tsdf_version(void) { return TSDF_ABI_VERSION; }
+
+uint64_t tsdf_workspace_bytes(void) { return 256; }
+
+static int check_device(int device)
+{
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= count) return fail(TSDF_ERR_INVALID, "device ordinal out of range");
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (major != 10) return fail(TSDF_ERR_UNSUPPORTED, "libnavi_tsdf is built for sm_100a (B200) only");
+    return TSDF_OK;
+}
+
+int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, uint32_t flags,
+                     tsdf_pool** out_pool)
+{
+    (void)flags;
+    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
+    *out_pool = nullptr;
+    if (!host_words && n_words) return fail(TSDF_ERR_INVALID, "words must not be null");
+    int rc = check_device(device);
+    if (rc != TSDF_OK) return rc;
+    tsdf::HostPool hp;
+    std::string err;
+    try {
+        rc = tsdf::build_host_pool(host_words, n_words, hp, err);
+    } catch (const std::bad_alloc&) {
+        return fail(TSDF_ERR_NO_MEMORY, "out of host memory while re-packing the DAG");
+    }
+    if (rc != TSDF_OK) return fail(rc, err);
+
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    auto* pool = new (std::nothrow) tsdf_pool();
+    if (!pool) return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+    pool->device = device;
+    pool->records = hp.recs.size() / 8;
+    pool->ext = hp.ext.size();
+    pool->source_words = n_words;
+    pool->root = hp.root;
+    pool->levels = hp.levels;
+    const size_t rec_bytes = std::max<size_t>(hp.recs.size() * sizeof(uint32_t), 32);
+    const size_t ext_bytes = std::max<size_t>(hp.ext.size() * sizeof(uint64_t), 8);
+    e = cudaMalloc(&pool->d_recs, rec_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&pool->d_ext, ext_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(pool->d_recs);
+        delete pool;
+        cudaGetLastError();
+        return fail(TSDF_ERR_NO_MEMORY, std::string("cudaMalloc for the node pool failed: ") +
+                                            cudaGetErrorString(e));
+    }
+    pool->bytes = rec_bytes + ext_bytes;
+    if (!hp.recs.empty())
+        e = cudaMemcpy(pool->d_recs, hp.recs.data(), hp.recs.size() * sizeof(uint32_t),
+                       cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && !hp.ext.empty())
+        e = cudaMemcpy(pool->d_ext, hp.ext.data(), hp.ext.size() * sizeof(uint64_t),
+                       cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(pool->d_recs);
+        cudaFree(pool->d_ext);
+        delete pool;
+        return cuda_fail(e, "cudaMemcpy of the node pool");
+    }
+    *out_pool = pool;
+    return TSDF_OK;
+}
+
+int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words, int device,
+                                 uint32_t flags, void* stream, tsdf_pool** out_pool)
+{
+    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
+    *out_pool = nullptr;
+    if (!device_words || n_words == 0) return fail(TSDF_ERR_LAYOUT, "DAG payload is empty");
+    int rc = check_device(device);
+    if (rc != TSDF_OK) return rc;
+    std::vector<uint64_t> host;
+    try {
+        host.resize(n_words);
+    } catch (const std::bad_alloc&) {
+        return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = cudaMemcpyAsync(host.data(), device_words, n_words * sizeof(uint64_t),
+                        cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "copying the DAG words to the host");
+    return tsdf_pool_create(host.data(), n_words, device, flags, out_pool);
+}
+
+int tsdf_pool_destroy(tsdf_pool* pool)
+{
+    if (!pool) return TSDF_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(pool->device);
+    cudaError_t e1 = cudaFree(pool->d_recs);
+    cudaError_t e2 = cudaFree(pool->d_ext);
+    cudaSetDevice(prev);
+    delete pool;
+    if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFree");
+    if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFree");
+    return TSDF_OK;
+}
+
+int tsdf_pool_stats_get(const tsdf_pool* pool, tsdf_pool_stats* out)
+{
+    if (!pool || !out) return fail(TSDF_ERR_INVALID, "pool and out must not be null");
+    std::memset(out, 0, sizeof *out);
+    out->source_words = pool->source_words;
+    out->records = pool->records;
+    out->ext_leaves = pool->ext;
+    out->device_bytes = pool->bytes;
+    out->root_slot = pool->root;
+    out->bfs_levels = pool->levels;
+    out->device = pool->device;
+    return TSDF_OK;
+}
+
+int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_min,
+                       const float* bbox_max, const float* hit_epsilon, tsdf_scenes** out)
+{
+    if (!out) return fail(TSDF_ERR_INVALID, "out must not be null");
+    *out = nullptr;
+    if (!pools || n <= 0 || !bbox_min || !bbox_max || !hit_epsilon)
+        return fail(TSDF_ERR_INVALID, "scene table needs n > 0 pools, bounds and epsilons");
+    const int device = pools[0] ? pools[0]->device : -1;
+    auto* sc = new (std::nothrow) tsdf_scenes();
+    if (!sc) return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+    sc->device = device;
+    sc->n = n;
+    sc->host.resize(n);
+    for (int i = 0; i < n; ++i) {
+        const tsdf_pool* p = pools[i];
+        if (!p || p->device != device) {
+            delete sc;
+            return fail(TSDF_ERR_INVALID, "every pool of a scene table must live on the same device");
+        }
+        TsdfSceneDev& d = sc->host[i];
+        d.recs = p->d_recs;
+        d.ext = p->d_ext;
+        d.root = p->root;
+        d.n_recs = static_cast<uint32_t>(p->records);
+        for (int a = 0; a < 3; ++a) {
+            d.bmin[a] = bbox_min[3 * i + a];
+            d.bmax[a] = bbox_max[3 * i + a];
+            if (!(d.bmin[a] < d.bmax[a])) {
+                delete sc;
+                return fail(TSDF_ERR_INVALID, "bbox_min entries must be strictly less than bbox_max entries");
+            }
+        }
+        d.eps = hit_epsilon[i];
+        d.pad_ = 0.0f;
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMalloc(&sc->d_table, sizeof(TsdfSceneDev) * n);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(sc->d_table, sc->host.data(), sizeof(TsdfSceneDev) * n, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(sc->d_table);
+        delete sc;
+        return cuda_fail(e, "uploading the scene table");
+    }
+    *out = sc;
+    return TSDF_OK;
+}
+
+int tsdf_scenes_destroy(tsdf_scenes* scenes)
+{
+    if (!scenes) return TSDF_OK;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(scenes->device);
+    cudaError_t e = cudaFree(scenes->d_table);
+    cudaSetDevice(prev);
+    delete scenes;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
+    return TSDF_OK;
+}
+
+}  // extern "C"

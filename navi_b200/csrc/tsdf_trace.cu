@@ -1,0 +1,492 @@
+// Batched sphere trace over the re-packed .gmdag node pool, sm_100a.
+//
+// Semantics: exactly those of the reference sphere_trace_kernel
+// (projects/torch-sdf/cpp_src/kernel.cu:203-309) and its stackless descent
+// (kernel.cu:88-200), per ray: the same float operations in the same order,
+// the same leaf / void / depth-4 prefix caches with the same inclusive or
+// strict bounds, the same 32-level descent cap.  The hit epsilon is a
+// parameter (0.01 in the reference) and the number of march iterations is an
+// extra output.
+//
+// Execution: a persistent grid (a few blocks per SM).  Each lane owns one ray
+// and runs a small state machine; one loop iteration performs either the start
+// of a march step (position update and cache tests, which often finish the
+// step) or one level of DAG descent (one 4-byte load), then the end of the
+// step if it finished.  Lanes whose ray has ended are refilled at the top of
+// the next iteration from a warp-local range of ray indices; the warp claims
+// ranges of `chunk` rays from a global counter with one atomicAdd, so short
+// rays never leave lanes idle while long rays march on.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+
+#include "tsdf_internal.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr unsigned kFull = 0xFFFFFFFFu;
+constexpr float kOutside = 1000.0f;      // kernel.cuh:8
+constexpr float kDirEps = 1e-4f;         // kernel.cuh:9
+constexpr float kVoidAdvance = 1e-5f;    // kernel.cu:9
+constexpr int kPrefixDepth = 4;          // kernel.cuh:11
+constexpr int kMaxDepth = 32;            // kernel.cu:136
+constexpr int64_t kMaxRays = (1ll << 31) - (1ll << 24);
+
+std::atomic<int64_t> g_smem_records{1024};
+std::atomic<int64_t> g_chunk{32};
+std::atomic<int64_t> g_blocks_per_sm{0};
+
+// lane flags
+constexpr uint32_t kVoidOk = 1u;
+constexpr uint32_t kLeafOk = 2u;
+constexpr uint32_t kPreOk = 4u;
+constexpr uint32_t kInDesc = 8u;
+constexpr uint32_t kUsePre = 16u;
+
+struct TraceArgs {
+    TsdfSceneDev scene;          // single-scene launches
+    const TsdfSceneDev* table;   // multi-scene launches
+    const float* origins;        // explicit rays [n][3]
+    const float* dirs;
+    const float4* poses;         // fan rays: 2 float4 per actor (tsdf_pose)
+    const float* fan;            // [rays_per_actor][3]
+    uint32_t rays_per_actor;
+    int use_pitch;
+    uint32_t n_rays;
+    int max_steps;
+    float max_distance;
+    uint32_t n_smem;             // records staged in shared memory
+    uint32_t chunk;
+    float* out_d;
+    int32_t* out_s;
+    int32_t* out_steps;
+    unsigned int* counter;
+};
+
+__device__ __forceinline__ bool in_closed(const float3 p, const float3 mn, const float3 mx)
+{
+    return p.x >= mn.x && p.x <= mx.x && p.y >= mn.y && p.y <= mx.y && p.z >= mn.z && p.z <= mx.z;
+}
+
+__device__ __forceinline__ bool in_open(const float3 p, const float3 mn, const float3 mx)
+{
+    return p.x > mn.x && p.x < mx.x && p.y > mn.y && p.y < mx.y && p.z > mn.z && p.z < mx.z;
+}
+
+// kernel.cu:54-85; divisions are IEEE round-to-nearest
+__device__ __forceinline__ float exit_distance(const float3 p, const float3 d, const float3 mn,
+                                               const float3 mx)
+{
+    float t = kOutside;
+    if (d.x > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mx.x, p.x), d.x));
+    else if (d.x < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mn.x, p.x), d.x));
+    if (d.y > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mx.y, p.y), d.y));
+    else if (d.y < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mn.y, p.y), d.y));
+    if (d.z > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mx.z, p.z), d.z));
+    else if (d.z < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(mn.z, p.z), d.z));
+    return fmaxf(t, kVoidAdvance);
+}
+
+__device__ __forceinline__ float leaf_distance(uint32_t bits)
+{
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
+}
+
+template <bool kFan, bool kMulti>
+__global__ void __launch_bounds__(kThreads) trace_kernel(const TraceArgs a)
+{
+    extern __shared__ __align__(16) uint32_t s_recs[];
+    const uint32_t n_smem = kMulti ? 0u : a.n_smem;
+    if (!kMulti && n_smem) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.scene.recs);
+        uint4* dst = reinterpret_cast<uint4*>(s_recs);
+        for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
+        __syncthreads();
+    }
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t lt_mask = (1u << lane) - 1u;
+
+    // warp-uniform work queue
+    uint32_t q_next = 0, q_end = 0;
+    bool exhausted = false;
+
+    // lane state
+    bool active = false;
+    uint32_t ray = 0;
+    float3 o = make_float3(0.f, 0.f, 0.f), d = o, p = o;
+    float t = 0.f, dist = 0.f;
+    int32_t sem = 0;
+    int step = 0;
+    uint32_t flags = 0;
+    float3 vmn = o, vmx = o, lmn = o, lmx = o, pmn = o, pmx = o, cmn = o, cmx = o;
+    float leaf_d = 0.f;
+    int32_t leaf_s = 0;
+    uint32_t pre_rec = 0, node = 0;
+    int depth = 0;
+
+    // scene of the lane's ray
+    const uint32_t* recs = a.scene.recs;
+    const uint64_t* ext = a.scene.ext;
+    uint32_t root = a.scene.root;
+    float3 bmn = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
+    float3 bmx = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
+    float eps = a.scene.eps;
+
+    for (;;) {
+        // ---- refill idle lanes from the warp queue ----
+        const unsigned idle = __ballot_sync(kFull, !active);
+        if (idle != 0u && !exhausted) {
+            const uint32_t nidle = __popc(idle);
+            const uint32_t rank = __popc(idle & lt_mask);
+            const uint32_t avail = q_end - q_next;
+            uint32_t mine = 0xFFFFFFFFu;
+            if (!active && rank < avail) mine = q_next + rank;
+            const uint32_t take = min(avail, nidle);
+            q_next += take;
+            if (nidle > take) {
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(a.counter, a.chunk);
+                base = __shfl_sync(kFull, base, 0);
+                if (base >= a.n_rays) {
+                    exhausted = true;
+                } else {
+                    q_next = base;
+                    q_end = min(base + a.chunk, a.n_rays);
+                    const uint32_t got = min(nidle - take, q_end - q_next);
+                    if (!active && rank >= take && rank - take < got) mine = q_next + (rank - take);
+                    q_next += got;
+                }
+            }
+            if (mine != 0xFFFFFFFFu) {
+                ray = mine;
+                active = true;
+                t = 0.f;
+                dist = 0.f;
+                sem = 0;
+                step = 0;
+                flags = 0;
+                if constexpr (kFan) {
+                    const uint32_t actor = mine / a.rays_per_actor;
+                    const uint32_t r = mine - actor * a.rays_per_actor;
+                    const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
+                    const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
+                    float bx = __ldg(a.fan + 3 * static_cast<size_t>(r));
+                    float by = __ldg(a.fan + 3 * static_cast<size_t>(r) + 1);
+                    float bz = __ldg(a.fan + 3 * static_cast<size_t>(r) + 2);
+                    if (a.use_pitch) {
+                        const float yp = __fsub_rn(__fmul_rn(by, p1.y), __fmul_rn(bz, p1.z));
+                        const float zp = __fadd_rn(__fmul_rn(by, p1.z), __fmul_rn(bz, p1.y));
+                        by = yp;
+                        bz = zp;
+                    }
+                    // sdfdag_backend.py:1303-1310, each product rounded on its own
+                    d.x = __fadd_rn(__fmul_rn(bx, p0.w), __fmul_rn(bz, p1.x));
+                    d.y = by;
+                    d.z = __fadd_rn(__fmul_rn(-bx, p1.x), __fmul_rn(bz, p0.w));
+                    o = make_float3(p0.x, p0.y, p0.z);
+                    if constexpr (kMulti) {
+                        const TsdfSceneDev* sc = a.table + __float_as_int(p1.w);
+                        recs = sc->recs;
+                        ext = sc->ext;
+                        root = sc->root;
+                        bmn = make_float3(sc->bmin[0], sc->bmin[1], sc->bmin[2]);
+                        bmx = make_float3(sc->bmax[0], sc->bmax[1], sc->bmax[2]);
+                        eps = sc->eps;
+                    }
+                } else {
+                    const float* po = a.origins + 3 * static_cast<size_t>(mine);
+                    const float* pd = a.dirs + 3 * static_cast<size_t>(mine);
+                    o = make_float3(__ldg(po), __ldg(po + 1), __ldg(po + 2));
+                    d = make_float3(__ldg(pd), __ldg(pd + 1), __ldg(pd + 2));
+                }
+            }
+        }
+        if (!__any_sync(kFull, active)) break;
+        if (!active) continue;
+
+        bool step_done = false;
+        if (!(flags & kInDesc)) {
+            // ---- start of a march step (kernel.cu:260-294) ----
+            p.x = __fmaf_rn(t, d.x, o.x);
+            p.y = __fmaf_rn(t, d.y, o.y);
+            p.z = __fmaf_rn(t, d.z, o.z);
+            if ((flags & kVoidOk) && in_open(p, vmn, vmx)) {
+                dist = exit_distance(p, d, vmn, vmx);
+                sem = 0;
+                step_done = true;
+            } else if (!in_closed(p, bmn, bmx)) {
+                dist = kOutside;
+                sem = 0;
+                step_done = true;
+            } else if ((flags & kLeafOk) && in_closed(p, lmn, lmx)) {
+                dist = leaf_d;
+                sem = leaf_s;
+                step_done = true;
+            } else if ((flags & kPreOk) && in_closed(p, pmn, pmx)) {
+                node = pre_rec;
+                depth = kPrefixDepth;
+                cmn = pmn;
+                cmx = pmx;
+                flags |= kInDesc | kUsePre;
+            } else {
+                node = root;
+                depth = 0;
+                cmn = bmn;
+                cmx = bmx;
+                flags = (flags | kInDesc) & ~kUsePre;
+            }
+        }
+        if (flags & kInDesc) {
+            // ---- one descent level (kernel.cu:136-198) ----
+            // `leaf` receives the low 32 bits of a leaf word (half distance, 16-bit semantic)
+            uint32_t leaf = 0;
+            bool is_leaf = false;
+            if (node & tsdf::kSlotLeafBit) {
+                leaf = node & ~tsdf::kSlotLeafBit;
+                is_leaf = true;
+            } else if (node & tsdf::kSlotExtBit) {
+                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(ext) +
+                                                   (node & tsdf::kSlotIndexMask)));
+                is_leaf = true;
+            } else {
+                if (depth == kPrefixDepth && !(flags & kUsePre)) {
+                    pre_rec = node;
+                    pmn = cmn;
+                    pmx = cmx;
+                    flags |= kPreOk;
+                }
+                const float mx_ = (cmn.x + cmx.x) * 0.5f;
+                const float my_ = (cmn.y + cmx.y) * 0.5f;
+                const float mz_ = (cmn.z + cmx.z) * 0.5f;
+                const bool ux = p.x >= mx_, uy = p.y >= my_, uz = p.z >= mz_;
+                const uint32_t oct = (ux ? 1u : 0u) | (uy ? 2u : 0u) | (uz ? 4u : 0u);
+                if (ux) cmn.x = mx_; else cmx.x = mx_;
+                if (uy) cmn.y = my_; else cmx.y = my_;
+                if (uz) cmn.z = mz_; else cmx.z = mz_;
+                const size_t si = static_cast<size_t>(node) * 8u + oct;
+                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(recs + si);
+                if (slot == tsdf::kSlotVoid) {
+                    vmn = cmn;
+                    vmx = cmx;
+                    flags |= kVoidOk;
+                    dist = exit_distance(p, d, vmn, vmx);
+                    sem = 0;
+                    step_done = true;
+                } else if (depth + 1 >= kMaxDepth) {
+                    step_done = true;  // cap reached: dist / sem keep their previous values
+                } else if (slot & tsdf::kSlotLeafBit) {
+                    leaf = slot & ~tsdf::kSlotLeafBit;
+                    is_leaf = true;
+                } else {
+                    node = slot;
+                    ++depth;
+                }
+            }
+            if (is_leaf) {
+                lmn = cmn;
+                lmx = cmx;
+                leaf_d = leaf_distance(leaf);
+                leaf_s = static_cast<int32_t>(leaf >> 16);
+                flags |= kLeafOk;
+                dist = leaf_d;
+                sem = leaf_s;
+                step_done = true;
+            }
+            if (step_done) flags &= ~kInDesc;
+        }
+        if (step_done) {
+            // ---- end of the march step (kernel.cu:297-304) ----
+            if (sem != 0 && dist < eps) {
+                a.out_d[ray] = t;
+                a.out_s[ray] = sem;
+                if (a.out_steps) a.out_steps[ray] = step + 1;
+                active = false;
+            } else {
+                t = t + dist;
+                ++step;
+                if (t > a.max_distance || step >= a.max_steps) {
+                    a.out_d[ray] = t;
+                    a.out_s[ray] = 0;
+                    if (a.out_steps) a.out_steps[ray] = step;
+                    active = false;
+                }
+            }
+        }
+    }
+}
+
+}  // namespace
+
+namespace {
+
+using tsdf::cuda_fail;
+using tsdf::fail;
+
+bool finite3(const float* v) { return std::isfinite(v[0]) && std::isfinite(v[1]) && std::isfinite(v[2]); }
+
+int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, float max_distance,
+                  void* workspace)
+{
+    if (n_rays < 0 || n_rays > kMaxRays)
+        return fail(TSDF_ERR_INVALID, "number of rays must be in [0, 2^31 - 2^24]");
+    if (max_steps <= 0) return fail(TSDF_ERR_INVALID, "max_steps must be a positive integer");
+    if (!std::isfinite(max_distance) || max_distance <= 0.0f)
+        return fail(TSDF_ERR_INVALID, "max_distance must be a finite positive float");
+    if (n_rays > 0 && (!out_d || !out_s)) return fail(TSDF_ERR_INVALID, "output pointers must not be null");
+    if (n_rays > 0 && !workspace) return fail(TSDF_ERR_INVALID, "workspace must not be null");
+    return TSDF_OK;
+}
+
+template <bool kFan, bool kMulti>
+int launch(TraceArgs& a, int device, void* workspace, cudaStream_t stream)
+{
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    const size_t smem = static_cast<size_t>(a.n_smem) * 32u;
+    auto kern = trace_kernel<kFan, kMulti>;
+    if (smem > 48u * 1024u) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    }
+    int per_sm = static_cast<int>(g_blocks_per_sm.load());
+    if (per_sm <= 0) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (per_sm <= 0) return fail(TSDF_ERR_INVALID, "trace kernel does not fit on an SM with this shared-memory stage");
+    }
+    const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
+    const int blocks = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(sms) * per_sm, need));
+    a.counter = static_cast<unsigned int*>(workspace);
+    e = cudaMemsetAsync(workspace, 0, sizeof(unsigned int), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    kern<<<blocks, kThreads, smem, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "trace kernel launch");
+    return TSDF_OK;
+}
+
+uint32_t clamp_chunk()
+{
+    const int64_t c = g_chunk.load();
+    return static_cast<uint32_t>(c < 1 ? 1 : (c > 1024 ? 1024 : c));
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, int64_t n_rays,
+              float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
+              float max_distance, const float bbox_min[3], const float bbox_max[3],
+              float hit_epsilon, void* workspace, void* stream)
+{
+    if (!pool) return fail(TSDF_ERR_INVALID, "pool must not be null");
+    int rc = common_checks(n_rays, out_dist, out_sem, max_steps, max_distance, workspace);
+    if (rc != TSDF_OK) return rc;
+    if (!bbox_min || !bbox_max) return fail(TSDF_ERR_INVALID, "bbox_min and bbox_max must contain exactly 3 floats");
+    if (!finite3(bbox_min) || !finite3(bbox_max))
+        return fail(TSDF_ERR_INVALID, "bbox_min and bbox_max must contain only finite floats");
+    for (int i = 0; i < 3; ++i)
+        if (!(bbox_min[i] < bbox_max[i]))
+            return fail(TSDF_ERR_INVALID, "bbox_min entries must be strictly less than bbox_max entries");
+    if (std::isnan(hit_epsilon)) return fail(TSDF_ERR_INVALID, "hit_epsilon must not be NaN");
+    if (n_rays == 0) return TSDF_OK;
+    if (!origins || !dirs) return fail(TSDF_ERR_INVALID, "origins and dirs must not be null");
+
+    TraceArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.scene.recs = pool->d_recs;
+    a.scene.ext = pool->d_ext;
+    a.scene.root = pool->root;
+    a.scene.n_recs = static_cast<uint32_t>(pool->records);
+    for (int i = 0; i < 3; ++i) {
+        a.scene.bmin[i] = bbox_min[i];
+        a.scene.bmax[i] = bbox_max[i];
+    }
+    a.scene.eps = hit_epsilon;
+    a.origins = origins;
+    a.dirs = dirs;
+    a.n_rays = static_cast<uint32_t>(n_rays);
+    a.max_steps = max_steps;
+    a.max_distance = max_distance;
+    a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
+                                                       static_cast<int64_t>(pool->records)));
+    a.chunk = clamp_chunk();
+    a.out_d = out_dist;
+    a.out_s = out_sem;
+    a.out_steps = out_steps;
+    return launch<false, false>(a, pool->device, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
+                  const float* fan_dirs, int64_t rays_per_actor, int use_pitch, float* out_dist,
+                  int32_t* out_sem, int32_t* out_steps, int max_steps, float max_distance,
+                  void* workspace, void* stream)
+{
+    if (!scenes || scenes->n <= 0) return fail(TSDF_ERR_INVALID, "scenes must not be null");
+    if (n_actors < 0 || rays_per_actor < 0) return fail(TSDF_ERR_INVALID, "sizes must not be negative");
+    if (rays_per_actor > 0 && n_actors > kMaxRays / rays_per_actor)
+        return fail(TSDF_ERR_INVALID, "number of rays must be in [0, 2^31 - 2^24]");
+    const int64_t n_rays = n_actors * rays_per_actor;
+    int rc = common_checks(n_rays, out_dist, out_sem, max_steps, max_distance, workspace);
+    if (rc != TSDF_OK) return rc;
+    if (n_rays == 0) return TSDF_OK;
+    if (!poses || !fan_dirs) return fail(TSDF_ERR_INVALID, "poses and fan_dirs must not be null");
+    if (reinterpret_cast<uintptr_t>(poses) % 16u != 0)
+        return fail(TSDF_ERR_INVALID, "poses must be 16-byte aligned");
+
+    TraceArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.poses = reinterpret_cast<const float4*>(poses);
+    a.fan = fan_dirs;
+    a.rays_per_actor = static_cast<uint32_t>(rays_per_actor);
+    a.use_pitch = use_pitch ? 1 : 0;
+    a.n_rays = static_cast<uint32_t>(n_rays);
+    a.max_steps = max_steps;
+    a.max_distance = max_distance;
+    a.chunk = clamp_chunk();
+    a.out_d = out_dist;
+    a.out_s = out_sem;
+    a.out_steps = out_steps;
+    if (scenes->n == 1) {
+        a.scene = scenes->host[0];
+        a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
+                                                           static_cast<int64_t>(a.scene.n_recs)));
+        return launch<true, false>(a, scenes->device, workspace, static_cast<cudaStream_t>(stream));
+    }
+    a.table = scenes->d_table;
+    a.scene = scenes->host[0];
+    return launch<true, true>(a, scenes->device, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
+{
+    if (!key) return fail(TSDF_ERR_INVALID, "key must not be null");
+    std::atomic<int64_t>* slot = nullptr;
+    if (std::strcmp(key, "smem_records") == 0) {
+        if (value < 0 || value > 6000) return fail(TSDF_ERR_INVALID, "smem_records must be in [0, 6000]");
+        slot = &g_smem_records;
+    } else if (std::strcmp(key, "chunk") == 0) {
+        if (value < 1 || value > 1024) return fail(TSDF_ERR_INVALID, "chunk must be in [1, 1024]");
+        slot = &g_chunk;
+    } else if (std::strcmp(key, "blocks_per_sm") == 0) {
+        if (value < 0 || value > 32) return fail(TSDF_ERR_INVALID, "blocks_per_sm must be in [0, 32]");
+        slot = &g_blocks_per_sm;
+    } else {
+        return fail(TSDF_ERR_INVALID, std::string("unknown option: ") + key);
+    }
+    const int64_t old = slot->exchange(value);
+    if (old_value) *old_value = old;
+    return TSDF_OK;
+}
+
+}  // extern "C"

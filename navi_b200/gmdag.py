@@ -1,0 +1,236 @@
+"""``.gmdag`` files: load, validate, write, and compile from a triangle mesh.
+
+File format (projects/voxel-dag/src/compiler.hpp:22-32, docs/GMDAG.md): a
+32-byte little-endian header ``<4sIIffffI`` = magic ``b"GDAG"``, version 1,
+resolution, bbox_min xyz, voxel size, node count; then ``node_count`` u64 words.
+A word with bit 63 set is a leaf (bits 0-15 half-float distance, bits 16-31
+semantic); otherwise bits 55-62 are the child mask and bits 0-31 the index of
+the child pointer table, whose entries' low 32 bits index child nodes.
+
+:func:`load_gmdag_asset` mirrors the reference loader
+(projects/environment/src/navi_environment/integration/voxel_dag.py:193-259)
+with the same checks and error texts; the layout validator mirrors
+``_validate_gmdag_dag_layout`` (voxel_dag.py:29-78) but walks the DAG with an
+explicit stack instead of recursion.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from . import _native
+
+__all__ = [
+    "GmDagAsset",
+    "load_gmdag_asset",
+    "validate_gmdag_layout",
+    "write_gmdag",
+    "compile_mesh",
+    "half_from_float_ref",
+]
+
+_HEADER_STRUCT = struct.Struct("<4sIIffffI")
+
+
+@dataclass(frozen=True, slots=True)
+class GmDagAsset:
+    """Loaded ``.gmdag`` asset metadata and node payload (voxel_dag.py:81-91)."""
+
+    path: Path
+    version: int
+    resolution: int
+    bbox_min: tuple[float, float, float]
+    bbox_max: tuple[float, float, float]
+    voxel_size: float
+    nodes: np.ndarray
+
+
+def validate_gmdag_layout(nodes: np.ndarray) -> None:
+    """Reject cycles, empty internal masks and out-of-range references reachable from word 0."""
+    nodes = np.asarray(nodes, dtype=np.uint64)
+    node_count = int(nodes.shape[0])
+    state = np.zeros(node_count, dtype=np.uint8)  # 0 new, 1 on stack, 2 done
+    if node_count == 0:
+        msg = "Invalid gmdag DAG layout: node index out of range: 0"
+        raise RuntimeError(msg)
+    # each stack entry: (node index, next child offset)
+    stack: list[list[int]] = [[0, 0]]
+    state[0] = 1
+    while stack:
+        top = stack[-1]
+        node_index = top[0]
+        word = int(nodes[node_index])
+        if (word >> 63) == 1:
+            state[node_index] = 2
+            stack.pop()
+            continue
+        mask = (word >> 55) & 0xFF
+        if mask == 0:
+            msg = f"Invalid gmdag DAG layout: internal node {node_index} has empty child mask"
+            raise RuntimeError(msg)
+        child_base = word & 0xFFFFFFFF
+        child_count = int(mask.bit_count())
+        if top[1] == 0:
+            if child_base >= node_count:
+                msg = (
+                    "Invalid gmdag DAG layout: child pointer table starts beyond payload "
+                    f"at index {child_base}"
+                )
+                raise RuntimeError(msg)
+            if child_base + child_count > node_count:
+                msg = (
+                    "Invalid gmdag DAG layout: child pointer table exceeds payload bounds "
+                    f"for node {node_index}"
+                )
+                raise RuntimeError(msg)
+        if top[1] >= child_count:
+            state[node_index] = 2
+            stack.pop()
+            continue
+        child_index = int(nodes[child_base + top[1]])
+        top[1] += 1
+        if child_index < 0 or child_index >= node_count:
+            msg = (
+                "Invalid gmdag DAG layout: child reference out of range "
+                f"({child_index}) from node {node_index}"
+            )
+            raise RuntimeError(msg)
+        if state[child_index] == 2:
+            continue
+        if state[child_index] == 1:
+            msg = f"Invalid gmdag DAG layout: cycle detected at node index {child_index}"
+            raise RuntimeError(msg)
+        state[child_index] = 1
+        stack.append([child_index, 0])
+
+
+def load_gmdag_asset(path: Path | str, *, validate_layout: bool = True) -> GmDagAsset:
+    """Load a ``.gmdag`` binary into metadata plus a contiguous node array."""
+    path = Path(path).expanduser().resolve()
+    if not path.exists():
+        msg = f"gmdag asset does not exist: {path}"
+        raise FileNotFoundError(msg)
+    with path.open("rb") as handle:
+        header_bytes = handle.read(_HEADER_STRUCT.size)
+        if len(header_bytes) != _HEADER_STRUCT.size:
+            msg = f"Invalid gmdag header in {path}"
+            raise RuntimeError(msg)
+        magic, version, resolution, bmin_x, bmin_y, bmin_z, voxel_size, node_count = (
+            _HEADER_STRUCT.unpack(header_bytes)
+        )
+        if magic != b"GDAG":
+            msg = f"Unsupported gmdag magic in {path}: {magic!r}"
+            raise RuntimeError(msg)
+        if version != 1:
+            msg = f"Unsupported gmdag version in {path}: {version}"
+            raise RuntimeError(msg)
+        if resolution <= 0:
+            msg = f"Invalid gmdag resolution in {path}: {resolution}"
+            raise RuntimeError(msg)
+        if not np.isfinite(voxel_size) or voxel_size <= 0.0:
+            msg = f"Invalid gmdag voxel size in {path}: {voxel_size}"
+            raise RuntimeError(msg)
+        if node_count <= 0:
+            msg = f"Invalid gmdag node count in {path}: {node_count}"
+            raise RuntimeError(msg)
+        if not all(np.isfinite(v) for v in (bmin_x, bmin_y, bmin_z)):
+            msg = f"Invalid gmdag bounds in {path}: non-finite bbox_min values detected"
+            raise RuntimeError(msg)
+        nodes = np.fromfile(handle, dtype=np.uint64, count=node_count)
+        if nodes.shape[0] != node_count:
+            msg = (
+                f"Invalid gmdag node payload in {path}: expected {node_count} nodes, "
+                f"found {nodes.shape[0]}"
+            )
+            raise RuntimeError(msg)
+        if handle.read(1):
+            msg = f"Invalid gmdag payload in {path}: trailing bytes detected"
+            raise RuntimeError(msg)
+    if validate_layout:
+        validate_gmdag_layout(nodes)
+    bbox_min = (float(bmin_x), float(bmin_y), float(bmin_z))
+    extent = float(voxel_size) * int(resolution)  # Python double, voxel_dag.py:244-250
+    bbox_max = (bbox_min[0] + extent, bbox_min[1] + extent, bbox_min[2] + extent)
+    return GmDagAsset(
+        path=path,
+        version=int(version),
+        resolution=int(resolution),
+        bbox_min=bbox_min,
+        bbox_max=bbox_max,
+        voxel_size=float(voxel_size),
+        nodes=np.ascontiguousarray(nodes),
+    )
+
+
+def write_gmdag(
+    path: Path | str,
+    nodes: np.ndarray,
+    resolution: int,
+    bbox_min: tuple[float, float, float] | np.ndarray,
+    voxel_size: float,
+) -> Path:
+    """Write header + payload exactly as compiler.cpp:680-697 does."""
+    path = Path(path)
+    nodes = np.ascontiguousarray(np.asarray(nodes, dtype=np.uint64))
+    header = _HEADER_STRUCT.pack(
+        b"GDAG", 1, int(resolution), float(bbox_min[0]), float(bbox_min[1]), float(bbox_min[2]),
+        float(voxel_size), int(nodes.shape[0]),
+    )
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    with tmp.open("wb") as fh:
+        fh.write(header)
+        fh.write(nodes.tobytes())
+    tmp.replace(path)
+    return path
+
+
+@dataclass(frozen=True)
+class CompiledMesh:
+    nodes: np.ndarray  # uint64 words
+    resolution: int
+    bbox_min: tuple[float, float, float]  # float32 values as compiled
+    bbox_max: tuple[float, float, float]
+    voxel_size: float
+
+
+def compile_mesh(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0) -> CompiledMesh:
+    """Compile a triangle mesh to DAG words with the native scene compiler."""
+    lib = _native.gmdag_lib()
+    v = np.ascontiguousarray(vertices, dtype=np.float32).reshape(-1, 3)
+    t = np.ascontiguousarray(triangles, dtype=np.uint32).reshape(-1, 3)
+    handle = ctypes.c_void_p()
+    rc = lib.gmdag_compile_mesh(
+        v.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(v.shape[0]),
+        t.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(t.shape[0]),
+        ctypes.c_uint32(resolution), ctypes.c_int(threads), ctypes.byref(handle),
+    )
+    if rc != 0:
+        raise RuntimeError(f"gmdag compile failed: {lib.gmdag_last_error().decode()}")
+    try:
+        n = int(lib.gmdag_result_num_words(handle))
+        words = np.empty(n, dtype=np.uint64)
+        lib.gmdag_result_copy_words(handle, words.ctypes.data_as(ctypes.c_void_p))
+        bmin = (ctypes.c_float * 3)()
+        bmax = (ctypes.c_float * 3)()
+        vox = ctypes.c_float()
+        lib.gmdag_result_header(handle, bmin, bmax, ctypes.byref(vox))
+    finally:
+        lib.gmdag_result_free(handle)
+    return CompiledMesh(
+        nodes=words,
+        resolution=int(resolution),
+        bbox_min=(bmin[0], bmin[1], bmin[2]),
+        bbox_max=(bmax[0], bmax[1], bmax[2]),
+        voxel_size=float(vox.value),
+    )
+
+
+def half_from_float_ref(x: float) -> int:
+    """The scene compiler's float->half conversion (truncating; tiny values become +inf)."""
+    return int(_native.gmdag_lib().gmdag_half_from_float(ctypes.c_float(x)))

@@ -1,0 +1,323 @@
+"""CUDA path vs the oracle and vs the reference's own kernel, bit for bit.
+
+Tolerance: none.  Distances are compared as float32 bit patterns, semantics
+and step counts as integers.  The CUDA path is called through the C ABI
+(libnavi_tsdf.so) via navi_b200.tracer and the drop-in torch_sdf.cast_rays.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import torch_sdf
+from navi_b200 import scenes, tracer, workloads
+from oracle import oracle as O
+from tests.gpu_util import assert_bits_equal, assert_equal, cast_explicit, dev, eager_world_rays
+from tests.kat_cases import kat_cases
+
+pytestmark = pytest.mark.gpu
+CASES = kat_cases()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
+def test_known_answers_through_cast_rays(case):
+    d = dev()
+    dag = torch.from_numpy(case.dag.view(np.int64)).to(d)
+    o = torch.tensor([case.origins], dtype=torch.float32, device=d)
+    v = torch.tensor([case.dirs], dtype=torch.float32, device=d)
+    out_d = torch.full(o.shape[:2], -7.0, dtype=torch.float32, device=d)
+    out_s = torch.full(o.shape[:2], -7, dtype=torch.int32, device=d)
+    out_k = torch.full(o.shape[:2], -7, dtype=torch.int32, device=d)
+    torch_sdf.cast_rays(dag, o, v, out_d, out_s, case.max_steps, case.max_distance, list(case.bbox_min),
+                        list(case.bbox_max), case.resolution, out_steps=out_k)
+    torch.cuda.synchronize()
+    got_d = out_d.cpu().numpy()[0]
+    got_s = out_s.cpu().numpy()[0]
+    case.check(got_d, got_s)
+    ref = O.trace(case.dag, case.bbox_min, case.bbox_max, np.array(case.origins), np.array(case.dirs),
+                  max_steps=case.max_steps, max_distance=case.max_distance)
+    assert_bits_equal(got_d, ref["dist"], "dist")
+    assert_equal(got_s, ref["sem"], "sem")
+    assert_equal(out_k.cpu().numpy()[0], ref["steps"], "steps")
+
+
+@pytest.mark.skipif(not O.reference_available(), reason="reference kernel not built")
+@pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
+def test_known_answers_match_reference_kernel(case):
+    d = dev()
+    kern = O.ReferenceKernel()
+    dag = torch.from_numpy(O.pad_words(case.dag).view(np.int64)).to(d)
+    o = torch.tensor(case.origins, dtype=torch.float32, device=d)
+    v = torch.tensor(case.dirs, dtype=torch.float32, device=d)
+    rd = torch.empty(o.shape[0], dtype=torch.float32, device=d)
+    rs = torch.empty(o.shape[0], dtype=torch.int32, device=d)
+    kern.cast(dag, o, v, rd, rs, max_steps=case.max_steps, max_distance=case.max_distance,
+              bbox_min=case.bbox_min, bbox_max=case.bbox_max, resolution=case.resolution)
+    got_d, got_s, _ = cast_explicit(case.dag, case.origins, case.dirs, max_steps=case.max_steps,
+                                    max_distance=case.max_distance, bbox_min=case.bbox_min, bbox_max=case.bbox_max)
+    assert_bits_equal(got_d, rd.cpu().numpy(), "dist vs reference kernel")
+    assert_equal(got_s, rs.cpu().numpy(), "sem vs reference kernel")
+
+
+def _config_rays(config: int, scene: int = 0, actors: int | None = None, resolution: int | None = None):
+    cs = workloads.compiled_scene(config, scene, resolution=resolution)
+    pb = workloads.poses_for(config, [cs], actors=actors)
+    fan = torch.from_numpy(workloads.fan_for(config)).to(dev())
+    poses = tracer.make_poses(torch.from_numpy(pb.position).to(dev()), torch.from_numpy(pb.yaw).to(dev()),
+                              torch.from_numpy(pb.pitch).to(dev()))
+    o, v = eager_world_rays(fan, poses, pitch=True)
+    return cs, fan, poses, o, v
+
+
+@pytest.mark.parametrize("eps_rule", ["config", "reference_0.01"])
+def test_config1_matches_oracle_and_reference_kernel(eps_rule):
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, o, v = _config_rays(1)
+    eps = cs.hit_epsilon if eps_rule == "config" else 0.01
+    got_d, got_s, got_k = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                                        bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=eps)
+    on, vn = o.cpu().numpy(), v.cpu().numpy()
+    ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, on, vn, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                  hit_epsilon=eps, fma=True)
+    assert_bits_equal(got_d, ref["dist"], "dist vs oracle")
+    assert_equal(got_s, ref["sem"], "sem vs oracle")
+    assert_equal(got_k, ref["steps"], "steps vs oracle")
+    if not O.reference_available():
+        pytest.skip("reference kernel not built")
+    kern = O.ReferenceKernel(eps_variant=(eps_rule == "config"))
+    dag = torch.from_numpy(O.pad_words(cs.words).view(np.int64)).to(dev())
+    rd = torch.empty(got_d.shape[0], dtype=torch.float32, device=dev())
+    rs = torch.empty(got_d.shape[0], dtype=torch.int32, device=dev())
+    kern.cast(dag, o, v, rd, rs, max_steps=cfg.max_steps, max_distance=cfg.max_distance, bbox_min=cs.bbox_min,
+              bbox_max=cs.bbox_max, resolution=cfg.resolution, hit_epsilon=eps)
+    assert_bits_equal(got_d, rd.cpu().numpy(), "dist vs reference kernel")
+    assert_equal(got_s, rs.cpu().numpy(), "sem vs reference kernel")
+
+
+@pytest.mark.skipif(not O.reference_available(), reason="reference kernel not built")
+def test_reference_kernel_position_update_is_fused():
+    """Pins how the reference build evaluates o + t*d (kernel.cu:261-263): its outputs equal the
+    oracle with a fused multiply-add and differ from the two-rounding form on this workload."""
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, o, v = _config_rays(1)
+    kern = O.ReferenceKernel()
+    dag = torch.from_numpy(O.pad_words(cs.words).view(np.int64)).to(dev())
+    n = o.shape[0] * o.shape[1]
+    rd = torch.empty(n, dtype=torch.float32, device=dev())
+    rs = torch.empty(n, dtype=torch.int32, device=dev())
+    kern.cast(dag, o, v, rd, rs, max_steps=cfg.max_steps, max_distance=cfg.max_distance, bbox_min=cs.bbox_min,
+              bbox_max=cs.bbox_max, resolution=cfg.resolution)
+    on, vn = o.cpu().numpy(), v.cpu().numpy()
+    fused = O.trace(cs.words, cs.bbox_min, cs.bbox_max, on, vn, max_steps=cfg.max_steps,
+                    max_distance=cfg.max_distance, fma=True)
+    unfused = O.trace(cs.words, cs.bbox_min, cs.bbox_max, on, vn, max_steps=cfg.max_steps,
+                      max_distance=cfg.max_distance, fma=False)
+    ref_d = rd.cpu().numpy()
+    assert_bits_equal(ref_d, fused["dist"], "reference kernel vs fused-update oracle")
+    n_diff = int(np.sum(ref_d.view(np.uint32) != unfused["dist"].view(np.uint32)))
+    print(f"two-rounding oracle differs on {n_diff} of {n} rays")
+    assert n_diff > 0
+
+
+def test_fan_matches_explicit_rays_bitwise():
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, o, v = _config_rays(1)
+    got_d, got_s, got_k = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                                        bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+    pool = tracer.NodePool.from_words(cs.words, dev())
+    sset = tracer.SceneSet([pool], [cs.bbox_min], [cs.bbox_max], [cs.hit_epsilon])
+    n = got_d.shape[0]
+    fd = torch.empty(n, dtype=torch.float32, device=dev())
+    fs = torch.empty(n, dtype=torch.int32, device=dev())
+    fk = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, fd, fs, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                    use_pitch=True, out_steps=fk)
+    torch.cuda.synchronize()
+    assert_bits_equal(fd.cpu().numpy(), got_d, "fan dist")
+    assert_equal(fs.cpu().numpy(), got_s, "fan sem")
+    assert_equal(fk.cpu().numpy(), got_k, "fan steps")
+
+
+def test_fan_without_pitch_equals_reference_yaw_only_rays():
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, _, _ = _config_rays(1)
+    o, v = eager_world_rays(fan, poses, pitch=False)
+    got_d, got_s, got_k = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                                        bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+    sset = tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                           [cs.hit_epsilon])
+    n = got_d.shape[0]
+    fd = torch.empty(n, dtype=torch.float32, device=dev())
+    fs = torch.empty(n, dtype=torch.int32, device=dev())
+    fk = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, fd, fs, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                    use_pitch=False, out_steps=fk)
+    torch.cuda.synchronize()
+    assert_bits_equal(fd.cpu().numpy(), got_d, "yaw-only fan dist")
+    assert_equal(fs.cpu().numpy(), got_s, "yaw-only fan sem")
+    assert_equal(fk.cpu().numpy(), got_k, "yaw-only fan steps")
+
+
+def test_config2_full_step_matches_oracle():
+    """Full benchmark step of config 2 (64 actors x 12,288 rays, 512^3) against the oracle."""
+    cfg = scenes.CONFIGS[2]
+    cs, fan, poses, o, v = _config_rays(2)
+    sset = tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                           [cs.hit_epsilon])
+    n = o.shape[0] * o.shape[1]
+    fd = torch.empty(n, dtype=torch.float32, device=dev())
+    fs = torch.empty(n, dtype=torch.int32, device=dev())
+    fk = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, fd, fs, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                    use_pitch=True, out_steps=fk)
+    torch.cuda.synchronize()
+    ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, o.cpu().numpy(), v.cpu().numpy(), max_steps=cfg.max_steps,
+                  max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+    assert_bits_equal(fd.cpu().numpy(), ref["dist"], "dist")
+    assert_equal(fs.cpu().numpy(), ref["sem"], "sem")
+    assert_equal(fk.cpu().numpy(), ref["steps"], "steps")
+
+
+def test_multiscene_fan_matches_per_scene_oracle():
+    """Config-3 style scenes (rods) at 128^3, three scenes resident together, actors assigned at random."""
+    cfg = scenes.CONFIGS[3]
+    scene_list = [workloads.compiled_scene(3, s, resolution=128) for s in range(3)]
+    pb = workloads.poses_for(3, scene_list, actors=48)
+    fan_np = workloads.fan_for(3)
+    fan = torch.from_numpy(fan_np).to(dev())
+    d = dev()
+    poses = tracer.make_poses(torch.from_numpy(pb.position).to(d), torch.from_numpy(pb.yaw).to(d),
+                              torch.from_numpy(pb.pitch).to(d), torch.from_numpy(pb.scene).to(d))
+    pools = [tracer.NodePool.from_words(cs.words, d) for cs in scene_list]
+    sset = tracer.SceneSet(pools, [cs.bbox_min for cs in scene_list], [cs.bbox_max for cs in scene_list],
+                           [cs.hit_epsilon for cs in scene_list])
+    a, r = poses.shape[0], fan.shape[0]
+    fd = torch.empty(a * r, dtype=torch.float32, device=d)
+    fs = torch.empty(a * r, dtype=torch.int32, device=d)
+    fk = torch.empty(a * r, dtype=torch.int32, device=d)
+    tracer.cast_fan(sset, poses, fan, fd, fs, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                    use_pitch=False, out_steps=fk)
+    torch.cuda.synchronize()
+    o, v = eager_world_rays(fan, poses, pitch=False)
+    on, vn = o.cpu().numpy(), v.cpu().numpy()
+    fd_, fs_, fk_ = (x.cpu().numpy().reshape(a, r) for x in (fd, fs, fk))
+    assert len(set(pb.scene.tolist())) == 3
+    for s, cs in enumerate(scene_list):
+        m = pb.scene == s
+        ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, on[m], vn[m], max_steps=cfg.max_steps,
+                      max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+        assert_bits_equal(fd_[m], ref["dist"], f"scene {s} dist")
+        assert_equal(fs_[m], ref["sem"], f"scene {s} sem")
+        assert_equal(fk_[m], ref["steps"], f"scene {s} steps")
+
+
+def _grid_aligned_rays(cs, n: int, seed: int):
+    """Rays that start exactly on cell faces and run along axes (the inclusive/strict cache bounds matter)."""
+    rng = np.random.default_rng(seed)
+    lo = np.asarray(cs.bbox_min, np.float64)
+    vox = cs.voxel_size
+    res = cs.asset.resolution
+    idx = rng.integers(1, res - 1, size=(n, 3))
+    origins = (lo + idx * vox).astype(np.float32)
+    axes = rng.integers(0, 6, size=n)
+    dirs = np.zeros((n, 3), np.float32)
+    dirs[np.arange(n), axes % 3] = np.where(axes < 3, 1.0, -1.0)
+    return origins, dirs
+
+
+def test_edge_cases_grid_aligned_outside_and_tiny_components():
+    cfg = scenes.CONFIGS[1]
+    cs = workloads.compiled_scene(1)
+    o1, d1 = _grid_aligned_rays(cs, 3000, 1)
+    rng = np.random.default_rng(2)
+    # origins outside the domain, pointing in and out
+    o2 = rng.uniform(-5.0, 16.0, size=(2000, 3)).astype(np.float32)
+    d2 = rng.normal(size=(2000, 3)).astype(np.float32)
+    d2 /= np.linalg.norm(d2, axis=1, keepdims=True)
+    # direction components at and around the 1e-4 threshold of the exit distance
+    d3 = rng.normal(size=(2000, 3)).astype(np.float32)
+    d3[:, rng.integers(0, 3)] = rng.choice(np.array([0.0, 1e-4, -1e-4, 9.9e-5, 1.01e-4, -0.0], np.float32), 2000)
+    d3 /= np.linalg.norm(d3, axis=1, keepdims=True).astype(np.float32)
+    o3 = rng.uniform(0.0, 10.0, size=(2000, 3)).astype(np.float32)
+    origins = np.concatenate([o1, o2, o3])
+    dirs = np.concatenate([d1, d2, d3]).astype(np.float32)
+    for max_steps, horizon in ((1, 20.0), (cfg.max_steps, cfg.max_distance), (5000, 2000.0)):
+        got_d, got_s, got_k = cast_explicit(cs.words, origins, dirs, max_steps=max_steps, max_distance=horizon,
+                                            bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=0.01)
+        ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, origins, dirs, max_steps=max_steps, max_distance=horizon,
+                      hit_epsilon=0.01)
+        assert_bits_equal(got_d, ref["dist"], f"dist (max_steps={max_steps})")
+        assert_equal(got_s, ref["sem"], f"sem (max_steps={max_steps})")
+        assert_equal(got_k, ref["steps"], f"steps (max_steps={max_steps})")
+
+
+@pytest.mark.parametrize("n", [0, 1, 31, 33, 1000, 4097])
+def test_ragged_and_empty_batches(n):
+    cfg = scenes.CONFIGS[1]
+    cs = workloads.compiled_scene(1)
+    rng = np.random.default_rng(n)
+    origins = rng.uniform(0.5, 9.5, size=(n, 3)).astype(np.float32)
+    dirs = rng.normal(size=(n, 3)).astype(np.float32)
+    if n:
+        dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    got_d, got_s, got_k = cast_explicit(cs.words, origins.reshape(n, 3), dirs.reshape(n, 3), max_steps=cfg.max_steps,
+                                        max_distance=cfg.max_distance, bbox_min=cs.bbox_min, bbox_max=cs.bbox_max,
+                                        hit_epsilon=cs.hit_epsilon)
+    assert got_d.shape == (n,)
+    if n:
+        ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, origins, dirs, max_steps=cfg.max_steps,
+                      max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+        assert_bits_equal(got_d, ref["dist"], "dist")
+        assert_equal(got_s, ref["sem"], "sem")
+        assert_equal(got_k, ref["steps"], "steps")
+
+
+def test_repeated_casts_are_deterministic_and_overwrite_outputs():
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, o, v = _config_rays(1)
+    a = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance, bbox_min=cs.bbox_min,
+                      bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+    b = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance, bbox_min=cs.bbox_min,
+                      bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+    for x, y in zip(a, b):
+        assert np.array_equal(np.asarray(x).view(np.uint32), np.asarray(y).view(np.uint32))
+
+
+def test_cast_runs_on_the_callers_stream():
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, o, v = _config_rays(1)
+    d = dev()
+    pool = tracer.NodePool.from_words(cs.words, d)
+    n = o.shape[0] * o.shape[1]
+    s = torch.cuda.Stream(d)
+    out_d = torch.zeros(n, dtype=torch.float32, device=d)
+    out_s = torch.zeros(n, dtype=torch.int32, device=d)
+    s.wait_stream(torch.cuda.current_stream(d))
+    with torch.cuda.stream(s):
+        tracer.cast_rays_ex(pool, o, v, out_d, out_s, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                            bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+        done = torch.cuda.Event()
+        done.record(s)
+    done.synchronize()
+    ref = cast_explicit(cs.words, o, v, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                        bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon, pool=pool)
+    assert_bits_equal(out_d.cpu().numpy(), ref[0], "side-stream dist")
+
+
+def test_pool_cache_tracks_in_place_dag_updates():
+    d = dev()
+    from tests.kat_cases import leaf_word
+
+    dag = torch.from_numpy(np.array([leaf_word(0.005, 3)], np.uint64).view(np.int64)).to(d)
+    o = torch.tensor([[[0.5, 0.5, 0.5]]], device=d)
+    v = torch.tensor([[[0.0, 1.0, 0.0]]], device=d)
+    out_d = torch.zeros((1, 1), device=d)
+    out_s = torch.zeros((1, 1), dtype=torch.int32, device=d)
+    torch_sdf.cast_rays(dag, o, v, out_d, out_s, 4, 10.0, [0, 0, 0], [1, 1, 1], 1)
+    assert int(out_s.item()) == 3
+    dag.copy_(torch.from_numpy(np.array([leaf_word(0.5, 9)], np.uint64).view(np.int64)).to(d))
+    torch_sdf.cast_rays(dag, o, v, out_d, out_s, 1, 10.0, [0, 0, 0], [1, 1, 1], 1)
+    assert int(out_s.item()) == 0
+    assert abs(float(out_d.item()) - 0.5) < 1e-6
