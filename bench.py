@@ -45,14 +45,16 @@ FALLBACK_HBM_GBS = 6650.0
 def _args() -> argparse.Namespace:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["navi", "reference"], default="navi")
     ap.add_argument("--pose-sets", type=int, default=4, help="distinct pose sets cycled over the steps")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-actors", type=int, default=0, help="actors in the CPU-baseline sample (0 = auto)")
+    ap.add_argument("--descent", choices=["grid", "float"], default="grid",
+                    help="library descent: integer grid (default) or float; both give identical results")
     return ap.parse_args()
 
 
@@ -83,10 +85,16 @@ class ClockSampler:
         self._thread: threading.Thread | None = None
 
     def __enter__(self) -> "ClockSampler":
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ident = str(self.gpu)
+        if visible:
+            ids = [v.strip() for v in visible.split(",") if v.strip()]
+            if self.gpu < len(ids):
+                ident = ids[self.gpu]
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ident],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
             )
             self._thread = threading.Thread(target=self._read, daemon=True)
@@ -259,17 +267,22 @@ def _time_reference_kernel(cfg, scene_list, pb, fan, args) -> dict | None:
     out_s = torch.empty(n, dtype=torch.int32, device=dev)
     flush = torch.empty(2 * torch.cuda.get_device_properties(dev).L2_cache_size, dtype=torch.uint8, device=dev)
     ms = []
-    for i in range(args.warmup + max(3, min(args.steps, 10))):
+    legacy = torch.cuda.default_stream(dev)
+    for i in range(args.warmup + max(3, min(args.steps, 20))):
         flush.zero_()
         torch.cuda.synchronize()
-        t0 = time.perf_counter()
+        s0 = torch.cuda.Event(enable_timing=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        s0.record(legacy)
         kern.cast(dag, origins, dirs, out_d, out_s, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
                   bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, resolution=cfg.resolution,
                   hit_epsilon=cs.hit_epsilon)
+        e0.record(legacy)
+        torch.cuda.synchronize()
         if i >= args.warmup:
-            ms.append(1e3 * (time.perf_counter() - t0))
-    return {"value": n / (np.median(ms) / 1e3), "unit": UNIT, "ms_per_step": float(np.median(ms)),
-            "timing": "host wall clock around a synchronous launch on the legacy default stream (median)",
+            ms.append(s0.elapsed_time(e0))
+    return {"value": n / (float(np.mean(ms)) / 1e3), "unit": UNIT, "ms_per_step": float(np.mean(ms)),
+            "timing": "CUDA events on the legacy default stream around each launch (mean), L2 flushed between",
             "build": "oracle/_ref/libref_trace_eps.so: reference kernel.cu for sm_100a, kHitEpsilon settable"}
 
 
@@ -299,6 +312,7 @@ def run_navi(args) -> None:
     from navi_b200 import tracer
     from navi_b200.fan import build_spherical_ray_directions
 
+    tracer.set_option("descent", 0 if args.descent == "grid" else 1)
     # rank 0 compiles (and caches) the scenes first; the others then read the cache
     if dist is not None and rank != 0:
         dist.barrier()
@@ -327,17 +341,17 @@ def run_navi(args) -> None:
         tracer.cast_fan(sset, poses[k % len(poses)], fan, out_d, out_s, max_steps=cfg.max_steps,
                         max_distance=cfg.max_distance, use_pitch=use_pitch, out_steps=out_steps)
 
-    for k in range(args.warmup):
-        flush.zero_()
-        cast(k)
-    torch.cuda.synchronize(dev)
-
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        time.sleep(0.3)  # let nvidia-smi start sampling
+        for k in range(args.warmup):
+            flush.zero_()
+            cast(k)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
         wall0 = time.perf_counter()
         for k in range(args.steps):
             flush.zero_()
@@ -388,7 +402,7 @@ def run_navi(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = _cpu_baseline(args, cfg, scene_list, sets[0], fan_np)
+        cpu = _cpu_baseline(args, cfg, scene_list, sets[0], fan_np, poses[0].cpu().numpy())
 
     if rank == 0:
         value = total_rays / (job_ms / 1e3)
@@ -431,6 +445,7 @@ def run_navi(args) -> None:
                 "parallelism": f"dp{world} (scene replica per GPU, no hot-path collective)",
                 "l2": "flushed between steps (2 x L2 bytes written), outside the timed events",
                 "pool_bytes": int(sum(p.stats["device_bytes"] for p in pools)),
+                "descent": args.descent,
             },
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
@@ -554,7 +569,7 @@ def _e2e_fan(torch, tracer, args, cfg, sset, pb, fan, use_pitch, flush, dev) -> 
             "d2h_bytes_per_step": int(n * 12), "api": "navi_b200.tracer.cast_fan (host poses in, dist/sem/steps out)"}
 
 
-def _cpu_baseline(args, cfg, scene_list, pb, fan_np) -> dict:
+def _cpu_baseline(args, cfg, scene_list, pb, fan_np, poses_host) -> dict:
     """Reference algorithm on the host cores (oracle/ C restatement, OpenMP), on a bounded sample.
 
     Also returns the mean DAG word loads per ray (W_ref) of the sample, the
@@ -567,7 +582,8 @@ def _cpu_baseline(args, cfg, scene_list, pb, fan_np) -> dict:
     a = pb.position.shape[0]
     sample = args.cpu_sample_actors or max(1, min(a, 2 * cores))
     sel = np.arange(sample)
-    dirs = O.rotate_fan(fan_np, np.cos(pb.yaw[sel]), np.sin(pb.yaw[sel]), np.cos(pb.pitch[sel]), np.sin(pb.pitch[sel]))
+    ph = poses_host[sel]
+    dirs = O.rotate_fan(fan_np, ph[:, 3], ph[:, 4], ph[:, 5], ph[:, 6])
     origins = np.repeat(pb.position[sel][:, None, :], fan_np.shape[0], axis=1)
     loads = []
     rays = 0

@@ -67,6 +67,9 @@ GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gmdag_result_copy_words": (None, [c_void_p, c_void_p]),
     "gmdag_result_free": (None, [c_void_p]),
     "gmdag_half_from_float": (ctypes.c_uint16, [c_float]),
+    "gmdag_compute_sdf": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int, c_void_p,
+                                  ctypes.POINTER(c_float), ctypes.POINTER(c_float), ctypes.POINTER(c_float)]),
+    "gmdag_compile_grid": (c_int, [c_void_p, c_uint32, c_float, c_int, ctypes.POINTER(c_void_p)]),
 }
 
 

@@ -571,6 +571,67 @@ int gmdag_compile_mesh(const float* verts, uint64_t n_verts, const uint32_t* idx
     }
 }
 
+// Stage 2 only: dense unsigned SDF of a mesh on the compiler's grid, [res][res][res]
+// (z, y, x) into out_grid, with the bounds of stage 1.
+int gmdag_compute_sdf(const float* verts, uint64_t n_verts, const uint32_t* idx, uint64_t n_tri,
+                      uint32_t resolution, int n_threads, float* out_grid, float* bmin, float* bmax,
+                      float* voxel)
+{
+    g_err.clear();
+    if (!verts || !idx || !out_grid || n_verts == 0 || n_tri == 0 || resolution == 0 || resolution > 1024) {
+        g_err = "invalid arguments";
+        return -1;
+    }
+    for (uint64_t i = 0; i < 3 * n_tri; ++i)
+        if (idx[i] >= n_verts) {
+            g_err = "triangle index out of range";
+            return -1;
+        }
+    const int N = static_cast<int>(resolution);
+    mesh_bounds(verts, n_verts, resolution, bmin, bmax, voxel);
+    std::vector<float> grid(static_cast<size_t>(N) * N * N, std::numeric_limits<float>::max());
+    const float dx = (bmax[0] - bmin[0]) / N;
+    const float dy = (bmax[1] - bmin[1]) / N;
+    const float dz = (bmax[2] - bmin[2]) / N;
+    const float h = std::min({dx, dy, dz});
+    seed_triangles(grid, N, bmin, dx, dy, dz, h, verts, idx, n_tri, n_threads);
+    fast_sweep(grid, N, h, n_threads);
+    std::memcpy(out_grid, grid.data(), grid.size() * sizeof(float));
+    return 0;
+}
+
+// Stage 3 only: DAG words of a dense grid [res][res][res] (z, y, x) with the given voxel size.
+int gmdag_compile_grid(const float* grid_in, uint32_t resolution, float voxel, int n_threads, void** out)
+{
+    g_err.clear();
+    if (!grid_in || !out || resolution == 0 || resolution > 4096) {
+        g_err = "invalid arguments";
+        return -1;
+    }
+    *out = nullptr;
+    try {
+        const int N = static_cast<int>(resolution);
+        std::vector<float> grid(grid_in, grid_in + static_cast<size_t>(N) * N * N);
+        auto res = std::make_unique<CompileResult>();
+        res->resolution = resolution;
+        res->voxel = voxel;
+        for (int a = 0; a < 3; ++a) {
+            res->bmin[a] = 0.0f;
+            res->bmax[a] = voxel * static_cast<float>(N);
+        }
+        Pyramid pyr;
+        const bool use_pyr = Pyramid::is_pow2(N) && N > 1;
+        if (use_pyr) pyr.build(grid, N, n_threads);
+        DagBuilder b(grid, N, voxel, use_pyr ? &pyr : nullptr);
+        res->words = b.run();
+        *out = res.release();
+        return 0;
+    } catch (const std::bad_alloc&) {
+        g_err = "out of host memory while compiling";
+        return -3;
+    }
+}
+
 uint64_t gmdag_result_num_words(const void* r)
 {
     return r ? static_cast<const CompileResult*>(r)->words.size() : 0;

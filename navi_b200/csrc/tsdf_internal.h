@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -30,12 +31,21 @@ inline uint32_t encode_leaf_inline(uint64_t word)
     return kSlotLeafBit | (sem << 16) | static_cast<uint32_t>(word & 0xFFFFu);
 }
 
+// Deepest grid the integer descent supports: 2^12 cells per axis.
+constexpr int kMaxGridDepth = 12;
+
 struct HostPool {
     std::vector<uint32_t> recs;      // 8 per record
     std::vector<uint64_t> ext;       // out-of-line leaf words
     uint32_t root = kSlotVoid;
     uint32_t levels = 0;
+    int32_t height = 0;              // records on the longest root path; -1 if the graph has a cycle
 };
+
+// Per-axis grid lines of the reference's midpoint rule: B[0] = lo, B[2^D] = hi, and for
+// every cell [B[a], B[b]] met by the descent its midpoint B[(a+b)/2] = (B[a] + B[b]) * 0.5f
+// (kernel.cu:166-176).  Returns false when the lines are not strictly increasing.
+bool build_grid_lines(float lo, float hi, int depth, float* out);
 
 // Re-pack .gmdag words; returns TSDF_OK or an error with `err` set.
 int build_host_pool(const uint64_t* words, uint64_t n, HostPool& out, std::string& err);
@@ -44,6 +54,7 @@ int build_host_pool(const uint64_t* words, uint64_t n, HostPool& out, std::strin
 
 struct tsdf_pool {
     int device = 0;
+    int32_t height = 0;              // -1: cyclic record graph
     uint32_t* d_recs = nullptr;      // [records][8]
     uint64_t* d_ext = nullptr;       // [ext leaves]
     uint64_t records = 0;
@@ -52,25 +63,33 @@ struct tsdf_pool {
     uint64_t bytes = 0;
     uint32_t root = tsdf::kSlotVoid;
     uint32_t levels = 0;
+    // last bounding box checked for strictly increasing grid lines (tsdf_cast)
+    std::mutex grid_mu;
+    float grid_bmin[3] = {0.f, 0.f, 0.f};
+    float grid_bmax[3] = {0.f, 0.f, 0.f};
+    int grid_ok = -1;  // -1 unknown, 0 float descent, 1 grid descent
 };
 
 // Device view of one scene (fan casts index a table of these).
 struct TsdfSceneDev {
     const uint32_t* recs;
     const uint64_t* ext;
+    const float* lines;              // [3][2^depth + 1] grid lines, or null (float descent)
     uint32_t root;
     uint32_t n_recs;
     float bmin[3];
     float bmax[3];
     float eps;
-    float pad_;
+    int32_t depth;                   // grid depth D (cells per axis 2^D); -1: float descent
 };
-static_assert(sizeof(TsdfSceneDev) == 56, "scene record layout");
+static_assert(sizeof(TsdfSceneDev) == 64, "scene record layout");
 
 struct tsdf_scenes {
     int device = 0;
     int n = 0;
+    bool grid = false;               // every scene supports the integer descent
     TsdfSceneDev* d_table = nullptr;
+    float* d_lines = nullptr;
     std::vector<TsdfSceneDev> host;
 };
 

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <deque>
 #include <new>
@@ -127,7 +128,60 @@ int build_host_pool(const uint64_t* w, uint64_t n, HostPool& hp, std::string& er
         hp.recs.insert(hp.recs.end(), slots, slots + 8);
     }
     hp.levels = rec_node.empty() ? 0 : max_level + 1;
+
+    // height of every record (longest chain of records below it), iterative DFS;
+    // a back edge means a cycle, which only the float descent (32-level cap) handles
+    const size_t nr = rec_node.size();
+    hp.height = 0;
+    if (nr > 0) {
+        std::vector<int32_t> h(nr, 0);
+        std::vector<uint8_t> state(nr, 0);  // 0 new, 1 open, 2 done
+        std::vector<std::pair<uint32_t, int>> st;
+        st.emplace_back(0u, 0);
+        state[0] = 1;
+        bool cyclic = false;
+        while (!st.empty() && !cyclic) {
+            auto& top = st.back();
+            const uint32_t r = top.first;
+            if (top.second == 8) {
+                int32_t best = 0;
+                for (int o = 0; o < 8; ++o) {
+                    const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + o];
+                    if (sl != kSlotVoid && !(sl & (kSlotLeafBit | kSlotExtBit))) best = std::max(best, h[sl]);
+                }
+                h[r] = best + 1;
+                state[r] = 2;
+                st.pop_back();
+                continue;
+            }
+            const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + top.second];
+            ++top.second;
+            if (sl == kSlotVoid || (sl & (kSlotLeafBit | kSlotExtBit))) continue;
+            if (state[sl] == 1) {
+                cyclic = true;
+            } else if (state[sl] == 0) {
+                state[sl] = 1;
+                st.emplace_back(sl, 0);
+            }
+        }
+        hp.height = cyclic ? -1 : h[0];
+    }
     return TSDF_OK;
+}
+
+bool build_grid_lines(float lo, float hi, int depth, float* out)
+{
+    const int n = 1 << depth;
+    out[0] = lo;
+    out[n] = hi;
+    for (int lvl = 0; lvl < depth; ++lvl) {
+        const int stride = n >> lvl;
+        const int half = stride >> 1;
+        for (int a = 0; a < n; a += stride) out[a + half] = (out[a] + out[a + stride]) * 0.5f;
+    }
+    for (int k = 0; k < n; ++k)
+        if (!(out[k] < out[k + 1])) return false;
+    return true;
 }
 
 }  // namespace tsdf
@@ -184,6 +238,7 @@ int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, u
     pool->source_words = n_words;
     pool->root = hp.root;
     pool->levels = hp.levels;
+    pool->height = hp.height;
     const size_t rec_bytes = std::max<size_t>(hp.recs.size() * sizeof(uint32_t), 32);
     const size_t ext_bytes = std::max<size_t>(hp.ext.size() * sizeof(uint64_t), 8);
     e = cudaMalloc(&pool->d_recs, rec_bytes);
@@ -278,6 +333,9 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
     sc->device = device;
     sc->n = n;
     sc->host.resize(n);
+    std::vector<float> lines;
+    std::vector<size_t> line_off(n, 0);
+    bool grid = true;
     for (int i = 0; i < n; ++i) {
         const tsdf_pool* p = pools[i];
         if (!p || p->device != device) {
@@ -285,6 +343,7 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
             return fail(TSDF_ERR_INVALID, "every pool of a scene table must live on the same device");
         }
         TsdfSceneDev& d = sc->host[i];
+        std::memset(&d, 0, sizeof d);
         d.recs = p->d_recs;
         d.ext = p->d_ext;
         d.root = p->root;
@@ -292,20 +351,39 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
         for (int a = 0; a < 3; ++a) {
             d.bmin[a] = bbox_min[3 * i + a];
             d.bmax[a] = bbox_max[3 * i + a];
-            if (!(d.bmin[a] < d.bmax[a])) {
+            if (!std::isfinite(d.bmin[a]) || !std::isfinite(d.bmax[a]) || !(d.bmin[a] < d.bmax[a])) {
                 delete sc;
-                return fail(TSDF_ERR_INVALID, "bbox_min entries must be strictly less than bbox_max entries");
+                return fail(TSDF_ERR_INVALID, "bbox_min entries must be finite and strictly less than bbox_max entries");
             }
         }
         d.eps = hit_epsilon[i];
-        d.pad_ = 0.0f;
+        d.depth = -1;
+        if (p->height >= 0 && p->height <= tsdf::kMaxGridDepth) {
+            const size_t m = (size_t(1) << p->height) + 1;
+            line_off[i] = lines.size();
+            lines.resize(lines.size() + 3 * m);
+            bool ok = true;
+            for (int a = 0; a < 3; ++a)
+                ok = ok && tsdf::build_grid_lines(d.bmin[a], d.bmax[a], p->height, &lines[line_off[i] + a * m]);
+            if (ok) d.depth = p->height;
+        }
+        grid = grid && d.depth >= 0;
     }
+    sc->grid = grid;
     cudaError_t e = cudaSetDevice(device);
-    if (e == cudaSuccess) e = cudaMalloc(&sc->d_table, sizeof(TsdfSceneDev) * n);
+    if (e == cudaSuccess && !lines.empty()) e = cudaMalloc(&sc->d_lines, lines.size() * sizeof(float));
+    if (e == cudaSuccess && !lines.empty())
+        e = cudaMemcpy(sc->d_lines, lines.data(), lines.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        for (int i = 0; i < n; ++i)
+            if (sc->host[i].depth >= 0) sc->host[i].lines = sc->d_lines + line_off[i];
+        e = cudaMalloc(&sc->d_table, sizeof(TsdfSceneDev) * n);
+    }
     if (e == cudaSuccess)
         e = cudaMemcpy(sc->d_table, sc->host.data(), sizeof(TsdfSceneDev) * n, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(sc->d_table);
+        cudaFree(sc->d_lines);
         delete sc;
         return cuda_fail(e, "uploading the scene table");
     }
@@ -320,6 +398,7 @@ int tsdf_scenes_destroy(tsdf_scenes* scenes)
     cudaGetDevice(&prev);
     cudaSetDevice(scenes->device);
     cudaError_t e = cudaFree(scenes->d_table);
+    cudaFree(scenes->d_lines);
     cudaSetDevice(prev);
     delete scenes;
     if (e != cudaSuccess) return cuda_fail(e, "cudaFree");

@@ -23,7 +23,9 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "tsdf_internal.h"
 
@@ -41,6 +43,7 @@ constexpr int64_t kMaxRays = (1ll << 31) - (1ll << 24);
 std::atomic<int64_t> g_smem_records{1024};
 std::atomic<int64_t> g_chunk{32};
 std::atomic<int64_t> g_blocks_per_sm{0};
+std::atomic<int64_t> g_descent{0};  // 0: integer grid where possible, 1: float descent only
 
 // lane flags
 constexpr uint32_t kVoidOk = 1u;
@@ -99,7 +102,7 @@ __device__ __forceinline__ float leaf_distance(uint32_t bits)
 }
 
 template <bool kFan, bool kMulti>
-__global__ void __launch_bounds__(kThreads) trace_kernel(const TraceArgs a)
+__global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a)
 {
     extern __shared__ __align__(16) uint32_t s_recs[];
     const uint32_t n_smem = kMulti ? 0u : a.n_smem;
@@ -321,6 +324,426 @@ __global__ void __launch_bounds__(kThreads) trace_kernel(const TraceArgs a)
     }
 }
 
+
+// ============================================================================
+// Integer-grid kernel (main path).
+//
+// The float bounds the reference computes during a descent (kernel.cu:166-176)
+// are a fixed set of per-axis grid lines: the root box's faces, and each cell's
+// midpoint (lo + hi) * 0.5f computed once from its two faces.  With D the
+// height of the record graph, the lines B[0..2^D] per axis are built once per
+// block into shared memory.  Each march step converts p to integer cell
+// coordinates (ix = largest k with B[k] <= p, plus "p lies on line ix"), after
+// which every test of the reference is an integer comparison with identical
+// outcome:
+//   p >= mid            <=>  ix >= mid index
+//   closed box test     <=>  lo <= ix && (ix < hi || (ix == hi && on line))
+//   strict box test     <=>  (lo < ix || (lo == ix && !on line)) && ix < hi
+// and a descent only extracts coordinate bits.  The reference starts every
+// descent at the root or at its cached depth-4 node; the path it then follows
+// is a function of the coordinates alone, so the descent here resumes at the
+// deepest record it shares with the lane's previous descent path (kept in
+// shared memory per lane), and replays the depth-4 cache update the reference
+// makes when it passes that level.
+// ============================================================================
+
+constexpr int kStackLevels = tsdf::kMaxGridDepth;
+constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
+constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
+constexpr int kLvShift = 16;             // 6 bits: level of the node being descended
+
+__device__ __forceinline__ uint32_t pack_cell(int j, int shift)
+{
+    const uint32_t lo = static_cast<uint32_t>((j >> shift) << shift);
+    return lo | ((lo + (1u << shift)) << 16);
+}
+
+__device__ __forceinline__ bool cell_closed(uint32_t c, int i, bool on)
+{
+    const int lo = static_cast<int>(c & 0xFFFFu), hi = static_cast<int>(c >> 16);
+    return lo <= i && (i < hi || (i == hi && on));
+}
+
+__device__ __forceinline__ bool cell_open(uint32_t c, int i, bool on)
+{
+    const int lo = static_cast<int>(c & 0xFFFFu), hi = static_cast<int>(c >> 16);
+    return (lo < i || (lo == i && !on)) && i < hi;
+}
+
+struct GridView {
+    const float* lines;  // [3][n + 1]
+    int n;
+};
+
+template <bool kShared>
+__device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
+{
+    const float* ptr = g.lines + axis * (g.n + 1) + k;
+    if constexpr (kShared) return *ptr;
+    else return __ldg(ptr);
+}
+
+// index of the last grid line <= p (-1 below the box, n at or above its top face)
+template <bool kShared>
+__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float b0, float bn,
+                                          float scale, bool& on)
+{
+    if (!(p >= b0)) {
+        on = false;
+        return -1;
+    }
+    if (p >= bn) {
+        on = (p == bn);
+        return g.n;
+    }
+    int k = min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n - 1);
+    float lo = line_at<kShared>(g, axis, k);
+    if (p < lo) {
+        do {
+            --k;
+            lo = line_at<kShared>(g, axis, k);
+        } while (p < lo);
+    } else {
+        float hi = line_at<kShared>(g, axis, k + 1);
+        while (p >= hi) {
+            ++k;
+            lo = hi;
+            hi = line_at<kShared>(g, axis, k + 1);
+        }
+    }
+    on = (p == lo);
+    return k;
+}
+
+// kernel.cu:54-85 with the void cell's faces read from the grid lines
+template <bool kShared>
+__device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
+                                                    uint32_t cx, uint32_t cy, uint32_t cz)
+{
+    float t = kOutside;
+    if (d.x > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 0, cx >> 16), p.x), d.x));
+    else if (d.x < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 0, cx & 0xFFFFu), p.x), d.x));
+    if (d.y > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 1, cy >> 16), p.y), d.y));
+    else if (d.y < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 1, cy & 0xFFFFu), p.y), d.y));
+    if (d.z > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 2, cz >> 16), p.z), d.z));
+    else if (d.z < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 2, cz & 0xFFFFu), p.z), d.z));
+    return fmaxf(t, kVoidAdvance);
+}
+
+// Claim rays for the idle lanes of the warp: returns this lane's new ray or ~0u.
+__device__ __forceinline__ uint32_t claim_ray(uint32_t& q_next, uint32_t& q_end, bool& exhausted, bool active,
+                                              uint32_t lane, unsigned int* counter, uint32_t chunk, uint32_t n_rays)
+{
+    const unsigned idle = __ballot_sync(kFull, !active);
+    uint32_t mine = 0xFFFFFFFFu;
+    if (idle == 0u || exhausted) return mine;
+    const uint32_t nidle = __popc(idle);
+    const uint32_t rank = __popc(idle & ((1u << lane) - 1u));
+    const uint32_t avail = q_end - q_next;
+    if (!active && rank < avail) mine = q_next + rank;
+    const uint32_t take = min(avail, nidle);
+    q_next += take;
+    if (nidle > take) {
+        uint32_t base = 0;
+        if (lane == 0) base = atomicAdd(counter, chunk);
+        base = __shfl_sync(kFull, base, 0);
+        if (base >= n_rays) {
+            exhausted = true;
+        } else {
+            q_next = base;
+            q_end = min(base + chunk, n_rays);
+            const uint32_t got = min(nidle - take, q_end - q_next);
+            if (!active && rank >= take && rank - take < got) mine = q_next + (rank - take);
+            q_next += got;
+        }
+    }
+    return mine;
+}
+
+// Ray `r`: explicit origin/direction, or fan ray (actor, local direction) with the
+// reference's rotation (sdfdag_backend.py:1303-1310) and the optional pitch.
+template <bool kFan>
+__device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3& o, float3& d, int& scene)
+{
+    if constexpr (kFan) {
+        const uint32_t actor = r / a.rays_per_actor;
+        const uint32_t k = r - actor * a.rays_per_actor;
+        const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
+        const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
+        float bx = __ldg(a.fan + 3 * static_cast<size_t>(k));
+        float by = __ldg(a.fan + 3 * static_cast<size_t>(k) + 1);
+        float bz = __ldg(a.fan + 3 * static_cast<size_t>(k) + 2);
+        if (a.use_pitch) {
+            const float yp = __fsub_rn(__fmul_rn(by, p1.y), __fmul_rn(bz, p1.z));
+            const float zp = __fadd_rn(__fmul_rn(by, p1.z), __fmul_rn(bz, p1.y));
+            by = yp;
+            bz = zp;
+        }
+        d.x = __fadd_rn(__fmul_rn(bx, p0.w), __fmul_rn(bz, p1.x));
+        d.y = by;
+        d.z = __fadd_rn(__fmul_rn(-bx, p1.x), __fmul_rn(bz, p0.w));
+        o = make_float3(p0.x, p0.y, p0.z);
+        scene = __float_as_int(p1.w);
+    } else {
+        const float* po = a.origins + 3 * static_cast<size_t>(r);
+        const float* pd = a.dirs + 3 * static_cast<size_t>(r);
+        o = make_float3(__ldg(po), __ldg(po + 1), __ldg(po + 2));
+        d = make_float3(__ldg(pd), __ldg(pd + 1), __ldg(pd + 2));
+        scene = 0;
+    }
+}
+
+template <bool kFan, bool kMulti, int kLevels>
+__global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
+{
+    constexpr bool kShared = !kMulti;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* s_stack = reinterpret_cast<uint32_t*>(smem_raw);   // [kStackLevels][kThreads]
+    uint32_t* s_recs = s_stack + kStackLevels * kThreads;           // [n_smem][8]
+    const uint32_t n_smem = kMulti ? 0u : a.n_smem;
+    float* s_lines = reinterpret_cast<float*>(s_recs + 8u * n_smem);  // [3][2^D + 1]
+
+    // scene of the lane's ray (uniform for single-scene launches)
+    const uint32_t* recs = a.scene.recs;
+    const uint64_t* ext = a.scene.ext;
+    uint32_t root = a.scene.root;
+    int D = a.scene.depth;
+    float eps = a.scene.eps;
+    float3 b0 = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
+    float3 bn = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
+    GridView g;
+    g.n = 1 << D;
+    g.lines = kShared ? s_lines : a.scene.lines;
+
+    if constexpr (!kMulti) {
+        if (n_smem) {
+            const uint4* src = reinterpret_cast<const uint4*>(recs);
+            uint4* dst = reinterpret_cast<uint4*>(s_recs);
+            for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
+        }
+        // grid lines by the midpoint rule, level by level
+        const int n = g.n;
+        if (threadIdx.x < 3) {
+            const unsigned ax = threadIdx.x;
+            s_lines[ax * (n + 1)] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
+            s_lines[ax * (n + 1) + n] = ax == 0 ? bn.x : (ax == 1 ? bn.y : bn.z);
+        }
+        __syncthreads();
+        for (int lvl = 0; lvl < D; ++lvl) {
+            const int stride = n >> lvl;
+            const int cells = 1 << lvl;
+            for (int w = threadIdx.x; w < 3 * cells; w += blockDim.x) {
+                const int axis = w / cells;
+                const int c = w - axis * cells;
+                float* row = s_lines + axis * (n + 1);
+                row[c * stride + (stride >> 1)] = (row[c * stride] + row[c * stride + stride]) * 0.5f;
+            }
+            __syncthreads();
+        }
+    }
+    float3 scale = make_float3(__fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.x, b0.x)),
+                               __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.y, b0.y)),
+                               __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.z, b0.z)));
+
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t* my_stack = s_stack + threadIdx.x;
+    uint32_t q_next = 0, q_end = 0;
+    bool exhausted = false;
+
+    bool active = false;
+    uint32_t ray = 0;
+    float3 o = make_float3(0.f, 0.f, 0.f), d = o;
+    float t = 0.f, dist = 0.f;
+    int32_t sem = 0;
+    int step = 0;
+    uint32_t flags = 0;
+    int jx = 0, jy = 0, jz = 0, jpx = 0, jpy = 0, jpz = 0;
+    uint32_t lcx = 0, lcy = 0, lcz = 0, vcx = 0, vcy = 0, vcz = 0, pcx = 0, pcy = 0, pcz = 0;
+    float leaf_d = 0.f;
+    int32_t leaf_s = 0;
+    uint32_t pre_rec = 0, node = 0;
+
+    for (;;) {
+        const uint32_t mine = claim_ray(q_next, q_end, exhausted, active, lane, a.counter, a.chunk, a.n_rays);
+        if (mine != 0xFFFFFFFFu) {
+            int scene = 0;
+            load_ray<kFan>(a, mine, o, d, scene);
+            ray = mine;
+            active = true;
+            t = 0.f;
+            dist = 0.f;
+            sem = 0;
+            step = 0;
+            flags = 0;
+            if constexpr (kMulti) {
+                const TsdfSceneDev* sc = a.table + scene;
+                recs = sc->recs;
+                ext = sc->ext;
+                root = sc->root;
+                D = sc->depth;
+                eps = sc->eps;
+                b0 = make_float3(sc->bmin[0], sc->bmin[1], sc->bmin[2]);
+                bn = make_float3(sc->bmax[0], sc->bmax[1], sc->bmax[2]);
+                g.n = 1 << D;
+                g.lines = sc->lines;
+                scale = make_float3(__fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.x, b0.x)),
+                                    __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.y, b0.y)),
+                                    __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.z, b0.z)));
+            }
+        }
+        if (!__any_sync(kFull, active)) break;
+        if (!active) continue;
+
+        bool step_done = false;
+        if (!(flags & kInDesc)) {
+            // ---- start of a march step (kernel.cu:260-294) ----
+            const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
+            bool ex, ey, ez;
+            const int ix = grid_index<kShared>(g, 0, p.x, b0.x, bn.x, scale.x, ex);
+            const int iy = grid_index<kShared>(g, 1, p.y, b0.y, bn.y, scale.y, ey);
+            const int iz = grid_index<kShared>(g, 2, p.z, b0.z, bn.z, scale.z, ez);
+            if ((flags & kVoidOk) && cell_open(vcx, ix, ex) && cell_open(vcy, iy, ey) && cell_open(vcz, iz, ez)) {
+                dist = cell_exit_distance<kShared>(g, p, d, vcx, vcy, vcz);
+                sem = 0;
+                step_done = true;
+            } else if (!(ix >= 0 && iy >= 0 && iz >= 0 && (ix < g.n || (ix == g.n && ex)) &&
+                         (iy < g.n || (iy == g.n && ey)) && (iz < g.n || (iz == g.n && ez)))) {
+                dist = kOutside;
+                sem = 0;
+                step_done = true;
+            } else if ((flags & kLeafOk) && cell_closed(lcx, ix, ex) && cell_closed(lcy, iy, ey) &&
+                       cell_closed(lcz, iz, ez)) {
+                dist = leaf_d;
+                sem = leaf_s;
+                step_done = true;
+            } else {
+                const bool use_pre = (flags & kPreOk) && cell_closed(pcx, ix, ex) && cell_closed(pcy, iy, ey) &&
+                                     cell_closed(pcz, iz, ez);
+                // descent coordinates: on the start box's top face the reference keeps taking the upper half
+                if (use_pre) {
+                    jx = min(ix, static_cast<int>(pcx >> 16) - 1);
+                    jy = min(iy, static_cast<int>(pcy >> 16) - 1);
+                    jz = min(iz, static_cast<int>(pcz >> 16) - 1);
+                } else {
+                    jx = min(ix, g.n - 1);
+                    jy = min(iy, g.n - 1);
+                    jz = min(iz, g.n - 1);
+                }
+                const int start = use_pre ? kPrefixDepth : 0;
+                const int sd = static_cast<int>((flags >> kSdShift) & 31u);
+                const int sv = (flags & kSvHigh) ? kPrefixDepth : 0;
+                const int common = D - 32 + __clz((jx ^ jpx) | (jy ^ jpy) | (jz ^ jpz));
+                const int reuse = min(common, sd - 1);
+                int level;
+                if (reuse >= start && reuse >= sv) {
+                    level = reuse;
+                    node = my_stack[level * kThreads];
+                    if (!use_pre && level > kPrefixDepth) {
+                        pre_rec = my_stack[kPrefixDepth * kThreads];
+                        pcx = pack_cell(jx, D - kPrefixDepth);
+                        pcy = pack_cell(jy, D - kPrefixDepth);
+                        pcz = pack_cell(jz, D - kPrefixDepth);
+                        flags |= kPreOk;
+                    }
+                } else {
+                    level = start;
+                    node = use_pre ? pre_rec : root;
+                    if (use_pre) flags |= kSvHigh;
+                    else flags &= ~kSvHigh;
+                }
+                flags = (flags & ~((63u << kLvShift) | kUsePre)) | kInDesc | (use_pre ? kUsePre : 0u) |
+                        (static_cast<uint32_t>(level) << kLvShift);
+            }
+        }
+#pragma unroll 1
+        for (int it = 0; it < kLevels && (flags & kInDesc); ++it) {
+            // ---- one descent level (kernel.cu:136-198) ----
+            int level = static_cast<int>((flags >> kLvShift) & 63u);
+            uint32_t leaf = 0;
+            int leaf_level = level;
+            bool is_leaf = false;
+            bool done = false;
+            if (node & tsdf::kSlotLeafBit) {
+                leaf = node & ~tsdf::kSlotLeafBit;
+                is_leaf = true;
+            } else if (node & tsdf::kSlotExtBit) {
+                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(ext) +
+                                                   (node & tsdf::kSlotIndexMask)));
+                is_leaf = true;
+            } else {
+                my_stack[level * kThreads] = node;
+                if (level == kPrefixDepth && !(flags & kUsePre)) {
+                    pre_rec = node;
+                    pcx = pack_cell(jx, D - kPrefixDepth);
+                    pcy = pack_cell(jy, D - kPrefixDepth);
+                    pcz = pack_cell(jz, D - kPrefixDepth);
+                    flags |= kPreOk;
+                }
+                const int sh = D - 1 - level;
+                const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
+                const size_t si = static_cast<size_t>(node) * 8u + oct;
+                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(recs + si);
+                leaf_level = level + 1;
+                if (slot == tsdf::kSlotVoid) {
+                    vcx = pack_cell(jx, D - leaf_level);
+                    vcy = pack_cell(jy, D - leaf_level);
+                    vcz = pack_cell(jz, D - leaf_level);
+                    flags |= kVoidOk;
+                    const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
+                    dist = cell_exit_distance<kShared>(g, p, d, vcx, vcy, vcz);
+                    sem = 0;
+                    done = true;
+                } else if (leaf_level >= kMaxDepth) {
+                    done = true;  // cap reached: dist / sem keep their previous values
+                } else if (slot & tsdf::kSlotLeafBit) {
+                    leaf = slot & ~tsdf::kSlotLeafBit;
+                    is_leaf = true;
+                } else {
+                    node = slot;
+                    flags = (flags & ~(63u << kLvShift)) | (static_cast<uint32_t>(leaf_level) << kLvShift);
+                }
+            }
+            if (is_leaf) {
+                lcx = pack_cell(jx, D - leaf_level);
+                lcy = pack_cell(jy, D - leaf_level);
+                lcz = pack_cell(jz, D - leaf_level);
+                leaf_d = leaf_distance(leaf);
+                leaf_s = static_cast<int32_t>(leaf >> 16);
+                flags |= kLeafOk;
+                dist = leaf_d;
+                sem = leaf_s;
+                done = true;
+            }
+            if (done) {
+                // records of levels 0..leaf_level-1 now lie on the path of (jx, jy, jz)
+                jpx = jx;
+                jpy = jy;
+                jpz = jz;
+                flags = (flags & ~(kInDesc | (31u << kSdShift))) | (static_cast<uint32_t>(leaf_level) << kSdShift);
+                step_done = true;
+            }
+        }
+        if (step_done) {
+            // ---- end of the march step (kernel.cu:297-304) ----
+            if (sem != 0 && dist < eps) {
+                a.out_d[ray] = t;
+                a.out_s[ray] = sem;
+                if (a.out_steps) a.out_steps[ray] = step + 1;
+                active = false;
+            } else {
+                t = t + dist;
+                ++step;
+                if (t > a.max_distance || step >= a.max_steps) {
+                    a.out_d[ray] = t;
+                    a.out_s[ray] = 0;
+                    if (a.out_steps) a.out_steps[ray] = step;
+                    active = false;
+                }
+            }
+        }
+    }
+}
+
 }  // namespace
 
 namespace {
@@ -343,16 +766,26 @@ int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, f
     return TSDF_OK;
 }
 
+enum class Kind { kFloat, kGrid };
+
 template <bool kFan, bool kMulti>
-int launch(TraceArgs& a, int device, void* workspace, cudaStream_t stream)
+int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream)
 {
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-    const size_t smem = static_cast<size_t>(a.n_smem) * 32u;
-    auto kern = trace_kernel<kFan, kMulti>;
+    void (*kern)(TraceArgs);
+    size_t smem;
+    if (kind == Kind::kGrid) {
+        kern = trace_grid_kernel<kFan, kMulti, 2>;
+        smem = static_cast<size_t>(kStackLevels) * kThreads * 4u + static_cast<size_t>(a.n_smem) * 32u;
+        if (!kMulti) smem += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 1u) * 4u;
+    } else {
+        kern = trace_float_kernel<kFan, kMulti>;
+        smem = static_cast<size_t>(a.n_smem) * 32u;
+    }
     if (smem > 48u * 1024u) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
@@ -372,6 +805,24 @@ int launch(TraceArgs& a, int device, void* workspace, cudaStream_t stream)
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "trace kernel launch");
     return TSDF_OK;
+}
+
+// Grid descent for this pool and box?  Cached per pool for the last box.
+bool pool_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
+{
+    if (g_descent.load() != 0) return false;
+    if (pool->height < 0 || pool->height > tsdf::kMaxGridDepth) return false;
+    std::lock_guard<std::mutex> lock(pool->grid_mu);
+    if (pool->grid_ok >= 0 && std::memcmp(pool->grid_bmin, bmin, sizeof pool->grid_bmin) == 0 &&
+        std::memcmp(pool->grid_bmax, bmax, sizeof pool->grid_bmax) == 0)
+        return pool->grid_ok == 1;
+    std::vector<float> lines((static_cast<size_t>(1) << pool->height) + 1);
+    bool ok = true;
+    for (int axis = 0; axis < 3 && ok; ++axis) ok = tsdf::build_grid_lines(bmin[axis], bmax[axis], pool->height, lines.data());
+    std::memcpy(pool->grid_bmin, bmin, sizeof pool->grid_bmin);
+    std::memcpy(pool->grid_bmax, bmax, sizeof pool->grid_bmax);
+    pool->grid_ok = ok ? 1 : 0;
+    return ok;
 }
 
 uint32_t clamp_chunk()
@@ -424,7 +875,10 @@ int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, in
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
-    return launch<false, false>(a, pool->device, workspace, static_cast<cudaStream_t>(stream));
+    const bool grid = pool_grid_ok(const_cast<tsdf_pool*>(pool), bbox_min, bbox_max);
+    a.scene.depth = grid ? pool->height : -1;
+    return launch<false, false>(grid ? Kind::kGrid : Kind::kFloat, a, pool->device, workspace,
+                                static_cast<cudaStream_t>(stream));
 }
 
 int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
@@ -461,11 +915,15 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
         a.scene = scenes->host[0];
         a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
                                                            static_cast<int64_t>(a.scene.n_recs)));
-        return launch<true, false>(a, scenes->device, workspace, static_cast<cudaStream_t>(stream));
+        const bool grid = scenes->grid && g_descent.load() == 0;
+        if (!grid) a.scene.depth = -1;
+        return launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace,
+                                   static_cast<cudaStream_t>(stream));
     }
     a.table = scenes->d_table;
     a.scene = scenes->host[0];
-    return launch<true, true>(a, scenes->device, workspace, static_cast<cudaStream_t>(stream));
+    return launch<true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
@@ -478,6 +936,9 @@ int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
     } else if (std::strcmp(key, "chunk") == 0) {
         if (value < 1 || value > 1024) return fail(TSDF_ERR_INVALID, "chunk must be in [1, 1024]");
         slot = &g_chunk;
+    } else if (std::strcmp(key, "descent") == 0) {
+        if (value < 0 || value > 1) return fail(TSDF_ERR_INVALID, "descent must be 0 (grid where possible) or 1 (float)");
+        slot = &g_descent;
     } else if (std::strcmp(key, "blocks_per_sm") == 0) {
         if (value < 0 || value > 32) return fail(TSDF_ERR_INVALID, "blocks_per_sm must be in [0, 32]");
         slot = &g_blocks_per_sm;

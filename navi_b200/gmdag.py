@@ -231,6 +231,43 @@ def compile_mesh(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *
     )
 
 
+def compute_sdf(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0):
+    """Stage 2 of the compiler alone: (dense grid [z, y, x] f32, bbox_min, bbox_max, voxel)."""
+    lib = _native.gmdag_lib()
+    v = np.ascontiguousarray(vertices, dtype=np.float32).reshape(-1, 3)
+    t = np.ascontiguousarray(triangles, dtype=np.uint32).reshape(-1, 3)
+    grid = np.empty((resolution, resolution, resolution), np.float32)
+    bmin = (ctypes.c_float * 3)()
+    bmax = (ctypes.c_float * 3)()
+    vox = ctypes.c_float()
+    rc = lib.gmdag_compute_sdf(v.ctypes.data_as(ctypes.c_void_p), v.shape[0], t.ctypes.data_as(ctypes.c_void_p),
+                               t.shape[0], resolution, threads, grid.ctypes.data_as(ctypes.c_void_p), bmin, bmax,
+                               ctypes.byref(vox))
+    if rc != 0:
+        raise RuntimeError(f"gmdag compute_sdf failed: {lib.gmdag_last_error().decode()}")
+    return grid, tuple(bmin), tuple(bmax), float(vox.value)
+
+
+def compile_grid(grid: np.ndarray, voxel_size: float, *, threads: int = 0) -> np.ndarray:
+    """Stage 3 of the compiler alone: DAG words of a dense grid [z, y, x]."""
+    lib = _native.gmdag_lib()
+    g = np.ascontiguousarray(grid, dtype=np.float32)
+    n = g.shape[0]
+    if g.shape != (n, n, n):
+        raise RuntimeError("grid must be cubic [res, res, res]")
+    handle = ctypes.c_void_p()
+    rc = lib.gmdag_compile_grid(g.ctypes.data_as(ctypes.c_void_p), n, ctypes.c_float(voxel_size), threads,
+                                ctypes.byref(handle))
+    if rc != 0:
+        raise RuntimeError(f"gmdag compile_grid failed: {lib.gmdag_last_error().decode()}")
+    try:
+        words = np.empty(int(lib.gmdag_result_num_words(handle)), dtype=np.uint64)
+        lib.gmdag_result_copy_words(handle, words.ctypes.data_as(ctypes.c_void_p))
+    finally:
+        lib.gmdag_result_free(handle)
+    return words
+
+
 def half_from_float_ref(x: float) -> int:
     """The scene compiler's float->half conversion (truncating; tiny values become +inf)."""
     return int(_native.gmdag_lib().gmdag_half_from_float(ctypes.c_float(x)))

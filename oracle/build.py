@@ -8,6 +8,9 @@
 - libref_trace.so: the reference's own kernel.cu, unmodified, compiled for
   sm_100a straight from the reference tree with the reference's nvcc flags
   (-O3 -lineinfo, projects/torch-sdf/setup.py:44) plus ref_shim.cu.
+- ref_voxel_dag: the reference scene compiler (projects/voxel-dag/src/compiler.cpp,
+  unmodified) built with g++ against oracle/assimp_standin/ (an OBJ-only
+  stand-in for the three Assimp headers it includes; Assimp is not available).
 - libref_trace_eps.so: the same kernel with kHitEpsilon turned into a run-time
   __constant__ (ref_shim_eps.cu says how).  The copied sources live in a
   scratch folder under oracle/_ref/ only while nvcc runs.
@@ -98,8 +101,26 @@ def build_reference(force: bool = False) -> list[Path]:
     return outs
 
 
+def build_reference_compiler(force: bool = False) -> list[Path]:
+    """The reference voxel-dag compiler (compiler.cpp, unmodified) + the Assimp stand-in headers."""
+    src = _reference_root() / "projects" / "voxel-dag" / "src"
+    if not (src / "compiler.cpp").exists():
+        return []
+    out = REF_OUT / "ref_voxel_dag"
+    standin = HERE / "assimp_standin"
+    deps = [src / "compiler.cpp", src / "compiler.hpp", HERE / "ref_compile_main.cpp",
+            *sorted((standin / "assimp").glob("*"))]
+    if force or _stale(out, deps):
+        REF_OUT.mkdir(parents=True, exist_ok=True)
+        cxx = _tool("/usr/bin/g++", os.environ.get("CXX"), shutil.which("g++"))
+        # default flags of a CMake Release build of the reference (no -ffast-math, no FMA target)
+        _run([cxx, "-O2", "-std=c++17", f"-I{standin}", f"-I{src}", str(src / "compiler.cpp"),
+              str(HERE / "ref_compile_main.cpp"), "-o", str(out)])
+    return [out]
+
+
 def build_all(force: bool = False) -> list[Path]:
-    return [build_oracle(force), *build_reference(force)]
+    return [build_oracle(force), *build_reference(force), *build_reference_compiler(force)]
 
 
 if __name__ == "__main__":

@@ -21,6 +21,14 @@ pytestmark = pytest.mark.gpu
 CASES = kat_cases()
 
 
+@pytest.fixture(params=["grid", "float"])
+def descent(request):
+    """Run a test under both descents of the library: integer grid (default) and float."""
+    old = tracer.set_option("descent", 0 if request.param == "grid" else 1)
+    yield request.param
+    tracer.set_option("descent", old)
+
+
 @pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
 def test_known_answers_through_cast_rays(case):
     d = dev()
@@ -72,7 +80,7 @@ def _config_rays(config: int, scene: int = 0, actors: int | None = None, resolut
 
 
 @pytest.mark.parametrize("eps_rule", ["config", "reference_0.01"])
-def test_config1_matches_oracle_and_reference_kernel(eps_rule):
+def test_config1_matches_oracle_and_reference_kernel(eps_rule, descent):
     cfg = scenes.CONFIGS[1]
     cs, fan, poses, o, v = _config_rays(1)
     eps = cs.hit_epsilon if eps_rule == "config" else 0.01
@@ -160,7 +168,7 @@ def test_fan_without_pitch_equals_reference_yaw_only_rays():
     assert_equal(fk.cpu().numpy(), got_k, "yaw-only fan steps")
 
 
-def test_config2_full_step_matches_oracle():
+def test_config2_full_step_matches_oracle(descent):
     """Full benchmark step of config 2 (64 actors x 12,288 rays, 512^3) against the oracle."""
     cfg = scenes.CONFIGS[2]
     cs, fan, poses, o, v = _config_rays(2)
@@ -180,7 +188,7 @@ def test_config2_full_step_matches_oracle():
     assert_equal(fk.cpu().numpy(), ref["steps"], "steps")
 
 
-def test_multiscene_fan_matches_per_scene_oracle():
+def test_multiscene_fan_matches_per_scene_oracle(descent):
     """Config-3 style scenes (rods) at 128^3, three scenes resident together, actors assigned at random."""
     cfg = scenes.CONFIGS[3]
     scene_list = [workloads.compiled_scene(3, s, resolution=128) for s in range(3)]
@@ -227,7 +235,7 @@ def _grid_aligned_rays(cs, n: int, seed: int):
     return origins, dirs
 
 
-def test_edge_cases_grid_aligned_outside_and_tiny_components():
+def test_edge_cases_grid_aligned_outside_and_tiny_components(descent):
     cfg = scenes.CONFIGS[1]
     cs = workloads.compiled_scene(1)
     o1, d1 = _grid_aligned_rays(cs, 3000, 1)
@@ -321,3 +329,58 @@ def test_pool_cache_tracks_in_place_dag_updates():
     torch_sdf.cast_rays(dag, o, v, out_d, out_s, 1, 10.0, [0, 0, 0], [1, 1, 1], 1)
     assert int(out_s.item()) == 0
     assert abs(float(out_d.item()) - 0.5) < 1e-6
+
+
+# ---------------------------------------------------------------- randomized DAGs
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_dags_match_oracle(seed):
+    from tests.dag_fuzz import random_dag, random_rays
+
+    rng = np.random.default_rng(1000 + seed)
+    depth = int(rng.integers(1, 9))
+    dag = random_dag(rng, depth)
+    if seed % 3 == 0:
+        bmin, bmax = (0.0, 0.0, 0.0), (1.0, 1.0, 1.0)
+    elif seed % 3 == 1:
+        bmin, bmax = (-3.25, 0.5, 7.0), (4.75, 2.0, 13.5)  # non-cubic box
+    else:
+        bmin, bmax = (-1.0, -1.0, -1.0), (11.0, 11.0, 11.0)
+    o, d = random_rays(rng, 6000, bmin, bmax, depth)
+    for eps, steps, horizon in ((0.01, 64, 30.0), (0.25, 7, 3.0)):
+        got_d, got_s, got_k = cast_explicit(dag, o, d, max_steps=steps, max_distance=horizon, bbox_min=bmin,
+                                            bbox_max=bmax, hit_epsilon=eps)
+        ref = O.trace(dag, bmin, bmax, o, d, max_steps=steps, max_distance=horizon, hit_epsilon=eps)
+        assert_bits_equal(got_d, ref["dist"], f"seed {seed} depth {depth} dist")
+        assert_equal(got_s, ref["sem"], f"seed {seed} sem")
+        assert_equal(got_k, ref["steps"], f"seed {seed} steps")
+
+
+def test_float_descent_fallback_deep_cyclic_and_degenerate():
+    """DAGs the integer grid does not cover: 14 levels deep, a cycle, and a box too thin for
+    distinct grid lines; all traced by the float-descent kernel, still bit-exact."""
+    from tests.dag_fuzz import random_rays
+    from tests.kat_cases import leaf_word, single_path_dag_words
+
+    rng = np.random.default_rng(7)
+    deep_octs = [int(x) for x in rng.integers(0, 8, size=14)]
+    deep = single_path_dag_words(deep_octs, distance=0.004, semantic=5)
+    cyclic = np.array([internal_word_(0b10000001, 1), 0, 3, leaf_word(0.003, 2)], np.uint64)
+    cases = [(deep, (0.0, 0.0, 0.0), (1.0, 1.0, 1.0)), (cyclic, (0.0, 0.0, 0.0), (1.0, 1.0, 1.0)),
+             (single_path_dag_words([1, 2, 3, 4, 5, 6], distance=0.5, semantic=1), (1e6, 0.0, 0.0),
+              (1e6 + 0.0625, 1.0, 1.0))]
+    for words, bmin, bmax in cases:
+        o, d = random_rays(rng, 3000, bmin, bmax, 6)
+        got_d, got_s, got_k = cast_explicit(words, o, d, max_steps=40, max_distance=5.0, bbox_min=bmin,
+                                            bbox_max=bmax)
+        ref = O.trace(words, bmin, bmax, o, d, max_steps=40, max_distance=5.0)
+        assert_bits_equal(got_d, ref["dist"], "dist")
+        assert_equal(got_s, ref["sem"], "sem")
+        assert_equal(got_k, ref["steps"], "steps")
+
+
+def internal_word_(mask: int, base: int) -> int:
+    from tests.kat_cases import internal_word
+
+    return internal_word(mask, base)
