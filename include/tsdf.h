@@ -130,7 +130,7 @@ TSDF_API int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, in
 
 /* Tuning knobs (process-wide): "smem_records" (records staged in shared
  * memory per block, default 1024), "chunk" (rays a warp claims at once,
- * default 32), "blocks_per_sm" (0 = occupancy maximum), "descent" (0 = integer
+ * default 8), "blocks_per_sm" (0 = occupancy maximum), "descent" (0 = integer
  * grid descent wherever the DAG allows it, 1 = float descent only; both give
  * the same results).  Returns the old value through *old_value when not NULL. */
 TSDF_API int tsdf_set_option(const char* key, int64_t value, int64_t* old_value);

@@ -41,7 +41,7 @@ constexpr int kMaxDepth = 32;            // kernel.cu:136
 constexpr int64_t kMaxRays = (1ll << 31) - (1ll << 24);
 
 std::atomic<int64_t> g_smem_records{1024};
-std::atomic<int64_t> g_chunk{32};
+std::atomic<int64_t> g_chunk{8};
 std::atomic<int64_t> g_blocks_per_sm{0};
 std::atomic<int64_t> g_descent{0};  // 0: integer grid where possible, 1: float descent only
 
