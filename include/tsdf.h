@@ -128,6 +128,20 @@ TSDF_API int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, in
                   float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
                   float max_distance, void* workspace, void* stream);
 
+/* Allocation-free variant of tsdf_cast (no counterpart in the reference): the
+ * same cast with no workspace argument, for callers that cannot allocate device
+ * memory while they run (a fixed-rate control loop must not stall in cudaMalloc;
+ * a host may hand the library only buffers registered up front).  Its scratch is
+ * a 256-byte static device array inside the library, held by every GPU that
+ * loads it; its address is looked up by the first call on each device, which
+ * must come before any stream capture.  All calls share that array: calls whose
+ * kernels may overlap on the GPU race and must be ordered on one stream.
+ * Allocates nothing: no cudaMalloc, no cudaFree. */
+TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, const float* dirs,
+                               int64_t n_rays, float* out_dist, int32_t* out_sem, int32_t* out_steps,
+                               int max_steps, float max_distance, const float bbox_min[3],
+                               const float bbox_max[3], float hit_epsilon, void* stream);
+
 /* Tuning knobs (process-wide): "smem_records" (records staged in shared
  * memory per block, default 1024), "chunk" (rays a warp claims at once,
  * default 8), "blocks_per_sm" (0 = occupancy maximum), "descent" (0 = integer

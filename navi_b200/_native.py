@@ -57,6 +57,8 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_cast_fan": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                               c_int, c_float, c_void_p, c_void_p]),
     "tsdf_set_option": (c_int, [c_char_p, c_int64, ctypes.POINTER(c_int64)]),
+    "tsdf_cast_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                                  c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p]),
 }
 
 GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {

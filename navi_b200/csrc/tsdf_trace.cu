@@ -951,3 +951,123 @@ int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Allocation-free cast.
+//
+// tsdf_cast needs a caller-provided device workspace (the work-queue counter of
+// the persistent kernel).  Some callers cannot allocate device memory once they
+// are running: a fixed-rate control loop (on the vehicle, say) must not stall in
+// cudaMalloc, which may synchronise the whole device, and a host that only
+// hands the library buffers it registered up front has nothing to hand over for
+// scratch.  tsdf_cast_noalloc takes no workspace: the counter lives in the
+// file-scope device array below, which every GPU that loads this library holds
+// until the process exits.
+//
+// Host code may not use the array's name as a device address (on the host it
+// names a stand-in object), so the address is fetched once per device with
+// cudaGetSymbolAddress, with that device current, by the first call on that
+// device.  Make that first call before any stream capture.  All calls on a
+// device share the array and it keeps the last call's contents: the counter is
+// cleared (cudaMemsetAsync on the caller's stream) before every launch, and two
+// calls whose kernels overlap on the GPU (different streams, no ordering between
+// them) race on it and produce wrong outputs; order them on one stream.
+// ============================================================================
+
+constexpr size_t kNoAllocScratchBytes = 256;  // stated maximum scratch of one cast
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+float g_noalloc_lines[(1 << tsdf::kMaxGridDepth) + 1];  // grid-line check buffer, under g_noalloc_mu
+
+// Same decision as pool_grid_ok, with a static buffer instead of a heap vector.
+bool noalloc_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
+{
+    if (g_descent.load() != 0) return false;
+    if (pool->height < 0 || pool->height > tsdf::kMaxGridDepth) return false;
+    std::lock_guard<std::mutex> lock(pool->grid_mu);
+    if (pool->grid_ok >= 0 && std::memcmp(pool->grid_bmin, bmin, sizeof pool->grid_bmin) == 0 &&
+        std::memcmp(pool->grid_bmax, bmax, sizeof pool->grid_bmax) == 0)
+        return pool->grid_ok == 1;
+    bool ok = true;
+    {
+        std::lock_guard<std::mutex> buf_lock(g_noalloc_mu);
+        for (int axis = 0; axis < 3 && ok; ++axis)
+            ok = tsdf::build_grid_lines(bmin[axis], bmax[axis], pool->height, g_noalloc_lines);
+    }
+    std::memcpy(pool->grid_bmin, bmin, sizeof pool->grid_bmin);
+    std::memcpy(pool->grid_bmax, bmax, sizeof pool->grid_bmax);
+    pool->grid_ok = ok ? 1 : 0;
+    return ok;
+}
+}  // namespace
+
+extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, const float* dirs,
+                                 int64_t n_rays, float* out_dist, int32_t* out_sem, int32_t* out_steps,
+                                 int max_steps, float max_distance, const float bbox_min[3],
+                                 const float bbox_max[3], float hit_epsilon, void* stream)
+{
+    if (!pool) return fail(TSDF_ERR_INVALID, "pool must not be null");
+    // the persistent kernel's only scratch is its work counter
+    const size_t need = sizeof(unsigned int);
+    if (need > kNoAllocScratchBytes)
+        return fail(TSDF_ERR_INVALID, "tsdf_cast_noalloc: the cast needs more scratch than the 256-byte static array");
+    if (pool->device < 0 || pool->device >= kNoAllocMaxDevices)
+        return fail(TSDF_ERR_INVALID, "tsdf_cast_noalloc supports device ordinals 0..63");
+    static int present;  // stands for the workspace argument this entry point does not take
+    int rc = common_checks(n_rays, out_dist, out_sem, max_steps, max_distance, &present);
+    if (rc != TSDF_OK) return rc;
+    if (!bbox_min || !bbox_max) return fail(TSDF_ERR_INVALID, "bbox_min and bbox_max must contain exactly 3 floats");
+    if (!finite3(bbox_min) || !finite3(bbox_max))
+        return fail(TSDF_ERR_INVALID, "bbox_min and bbox_max must contain only finite floats");
+    for (int i = 0; i < 3; ++i)
+        if (!(bbox_min[i] < bbox_max[i]))
+            return fail(TSDF_ERR_INVALID, "bbox_min entries must be strictly less than bbox_max entries");
+    if (std::isnan(hit_epsilon)) return fail(TSDF_ERR_INVALID, "hit_epsilon must not be NaN");
+    if (n_rays == 0) return TSDF_OK;
+    if (!origins || !dirs) return fail(TSDF_ERR_INVALID, "origins and dirs must not be null");
+
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_addr[pool->device]) {
+            cudaError_t e = cudaSetDevice(pool->device);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+            void* addr = nullptr;
+            e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+            g_noalloc_addr[pool->device] = addr;
+        }
+        scratch = g_noalloc_addr[pool->device];
+    }
+
+    TraceArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.scene.recs = pool->d_recs;
+    a.scene.ext = pool->d_ext;
+    a.scene.root = pool->root;
+    a.scene.n_recs = static_cast<uint32_t>(pool->records);
+    for (int i = 0; i < 3; ++i) {
+        a.scene.bmin[i] = bbox_min[i];
+        a.scene.bmax[i] = bbox_max[i];
+    }
+    a.scene.eps = hit_epsilon;
+    a.origins = origins;
+    a.dirs = dirs;
+    a.n_rays = static_cast<uint32_t>(n_rays);
+    a.max_steps = max_steps;
+    a.max_distance = max_distance;
+    a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
+                                                       static_cast<int64_t>(pool->records)));
+    a.chunk = clamp_chunk();
+    a.out_d = out_dist;
+    a.out_s = out_sem;
+    a.out_steps = out_steps;
+    const bool grid = noalloc_grid_ok(const_cast<tsdf_pool*>(pool), bbox_min, bbox_max);
+    a.scene.depth = grid ? pool->height : -1;
+    return launch<false, false>(grid ? Kind::kGrid : Kind::kFloat, a, pool->device, scratch,
+                                static_cast<cudaStream_t>(stream));
+}
