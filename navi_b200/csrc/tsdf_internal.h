@@ -44,7 +44,8 @@ struct HostPool {
 
 // Per-axis grid lines of the reference's midpoint rule: B[0] = lo, B[2^D] = hi, and for
 // every cell [B[a], B[b]] met by the descent its midpoint B[(a+b)/2] = (B[a] + B[b]) * 0.5f
-// (kernel.cu:166-176).  Returns false when the lines are not strictly increasing.
+// (kernel.cu:166-176); out has 2^D + 2 entries, the last one +inf.  Returns false when the
+// lines are not strictly increasing or the kernel's one-cell estimate bound does not hold.
 bool build_grid_lines(float lo, float hi, int depth, float* out);
 
 // Re-pack .gmdag words; returns TSDF_OK or an error with `err` set.
@@ -74,7 +75,7 @@ struct tsdf_pool {
 struct TsdfSceneDev {
     const uint32_t* recs;
     const uint64_t* ext;
-    const float* lines;              // [3][2^depth + 1] grid lines, or null (float descent)
+    const float* lines;              // [3][2^depth + 2] grid lines, or null (float descent)
     uint32_t root;
     uint32_t n_recs;
     float bmin[3];

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstring>
 #include <deque>
+#include <limits>
 #include <new>
 #include <string>
 #include <unordered_map>
@@ -174,6 +175,7 @@ bool build_grid_lines(float lo, float hi, int depth, float* out)
     const int n = 1 << depth;
     out[0] = lo;
     out[n] = hi;
+    out[n + 1] = std::numeric_limits<float>::infinity();  // padding read by the 3-line lookup
     for (int lvl = 0; lvl < depth; ++lvl) {
         const int stride = n >> lvl;
         const int half = stride >> 1;
@@ -181,6 +183,14 @@ bool build_grid_lines(float lo, float hi, int depth, float* out)
     }
     for (int k = 0; k < n; ++k)
         if (!(out[k] < out[k + 1])) return false;
+    // The kernel estimates the cell of p as floor(u(p)), u(p) = RN(RN(p - lo) * scale) with
+    // scale = RN(n / RN(hi - lo)), and then picks among cells e-1, e, e+1.  u is monotone in p,
+    // so |u(out[k]) - k| < 1 for every line k bounds the estimate within one cell everywhere.
+    const float scale = static_cast<float>(n) / (hi - lo);
+    for (int k = 0; k <= n; ++k) {
+        const float u = (out[k] - lo) * scale;
+        if (!(std::fabs(u - static_cast<float>(k)) < 1.0f)) return false;
+    }
     return true;
 }
 
@@ -359,7 +369,7 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
         d.eps = hit_epsilon[i];
         d.depth = -1;
         if (p->height >= 0 && p->height <= tsdf::kMaxGridDepth) {
-            const size_t m = (size_t(1) << p->height) + 1;
+            const size_t m = (size_t(1) << p->height) + 2;
             line_off[i] = lines.size();
             lines.resize(lines.size() + 3 * m);
             bool ok = true;

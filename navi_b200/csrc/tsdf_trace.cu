@@ -352,22 +352,26 @@ constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
 constexpr int kLvShift = 16;             // 6 bits: level of the node being descended
 
+// A cell of the finest grid's units: lo | size << 16 (size = 2^shift <= 4096).
 __device__ __forceinline__ uint32_t pack_cell(int j, int shift)
 {
-    const uint32_t lo = static_cast<uint32_t>((j >> shift) << shift);
-    return lo | ((lo + (1u << shift)) << 16);
+    return static_cast<uint32_t>((j >> shift) << shift) | (1u << (shift + 16));
 }
 
+__device__ __forceinline__ int cell_lo(uint32_t c) { return static_cast<int>(c & 0xFFFFu); }
+__device__ __forceinline__ int cell_hi(uint32_t c) { return static_cast<int>((c & 0xFFFFu) + (c >> 16)); }
+
+// closed box: lo <= i && (i < hi || (i == hi && on))  <=>  (i - lo) <u size + on
 __device__ __forceinline__ bool cell_closed(uint32_t c, int i, bool on)
 {
-    const int lo = static_cast<int>(c & 0xFFFFu), hi = static_cast<int>(c >> 16);
-    return lo <= i && (i < hi || (i == hi && on));
+    return static_cast<uint32_t>(i - cell_lo(c)) < (c >> 16) + (on ? 1u : 0u);
 }
 
+// strict box: (lo < i || (lo == i && !on)) && i < hi  <=>  (i - lo - on) <u size - on
 __device__ __forceinline__ bool cell_open(uint32_t c, int i, bool on)
 {
-    const int lo = static_cast<int>(c & 0xFFFFu), hi = static_cast<int>(c >> 16);
-    return (lo < i || (lo == i && !on)) && i < hi;
+    const uint32_t o = on ? 1u : 0u;
+    return static_cast<uint32_t>(i - cell_lo(c)) - o < (c >> 16) - o;
 }
 
 struct GridView {
@@ -378,55 +382,59 @@ struct GridView {
 template <bool kShared>
 __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
 {
-    const float* ptr = g.lines + axis * (g.n + 1) + k;
+    const float* ptr = g.lines + axis * (g.n + 2) + k;
     if constexpr (kShared) return *ptr;
     else return __ldg(ptr);
 }
 
-// index of the last grid line <= p (-1 below the box, n at or above its top face)
+// index of the last grid line <= p (-1 below the box, n at or above its top face).
+// e = floor(u(p)) is within one cell of the answer (proved per table on the host,
+// build_grid_lines), so three neighbouring lines decide it without a loop.
 template <bool kShared>
 __device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float b0, float bn,
                                           float scale, bool& on)
 {
+    const int e = max(min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n - 1), 1);
+    const float lm = line_at<kShared>(g, axis, e - 1);
+    const float l0 = line_at<kShared>(g, axis, e);
+    const float lp = line_at<kShared>(g, axis, e + 1);
+    const bool ge0 = p >= l0, gep = p >= lp;
+    int k = e - 1 + (ge0 ? 1 : 0) + (gep ? 1 : 0);
+    on = p == (gep ? lp : (ge0 ? l0 : lm));
     if (!(p >= b0)) {
         on = false;
-        return -1;
-    }
-    if (p >= bn) {
+        k = -1;
+    } else if (p >= bn) {
         on = (p == bn);
-        return g.n;
+        k = g.n;
     }
-    int k = min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n - 1);
-    float lo = line_at<kShared>(g, axis, k);
-    if (p < lo) {
-        do {
-            --k;
-            lo = line_at<kShared>(g, axis, k);
-        } while (p < lo);
-    } else {
-        float hi = line_at<kShared>(g, axis, k + 1);
-        while (p >= hi) {
-            ++k;
-            lo = hi;
-            hi = line_at<kShared>(g, axis, k + 1);
-        }
-    }
-    on = (p == lo);
     return k;
 }
 
-// kernel.cu:54-85 with the void cell's faces read from the grid lines
+// kernel.cu:54-85 with the void cell's faces read from the grid lines.  Approximate
+// quotients (within 2^-21 relative of the exact ones) pick the axes that can hold the
+// minimum; only those get the IEEE division, so the result is the reference's.
 template <bool kShared>
 __device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
                                                     uint32_t cx, uint32_t cy, uint32_t cz)
 {
+    const float inf = __int_as_float(0x7f800000);
+    float ax = 0.f, ay = 0.f, az = 0.f, qx = inf, qy = inf, qz = inf;
+    if (d.x > kDirEps) ax = __fsub_rn(line_at<kShared>(g, 0, cell_hi(cx)), p.x);
+    else if (d.x < -kDirEps) ax = __fsub_rn(line_at<kShared>(g, 0, cell_lo(cx)), p.x);
+    if (d.y > kDirEps) ay = __fsub_rn(line_at<kShared>(g, 1, cell_hi(cy)), p.y);
+    else if (d.y < -kDirEps) ay = __fsub_rn(line_at<kShared>(g, 1, cell_lo(cy)), p.y);
+    if (d.z > kDirEps) az = __fsub_rn(line_at<kShared>(g, 2, cell_hi(cz)), p.z);
+    else if (d.z < -kDirEps) az = __fsub_rn(line_at<kShared>(g, 2, cell_lo(cz)), p.z);
+    const bool vx = fabsf(d.x) > kDirEps, vy = fabsf(d.y) > kDirEps, vz = fabsf(d.z) > kDirEps;
+    if (vx) qx = __fdividef(ax, d.x);
+    if (vy) qy = __fdividef(ay, d.y);
+    if (vz) qz = __fdividef(az, d.z);
+    const float lim = __fmul_rn(fminf(fminf(qx, qy), qz), 1.0f + 0x1p-19f);
     float t = kOutside;
-    if (d.x > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 0, cx >> 16), p.x), d.x));
-    else if (d.x < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 0, cx & 0xFFFFu), p.x), d.x));
-    if (d.y > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 1, cy >> 16), p.y), d.y));
-    else if (d.y < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 1, cy & 0xFFFFu), p.y), d.y));
-    if (d.z > kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 2, cz >> 16), p.z), d.z));
-    else if (d.z < -kDirEps) t = fminf(t, __fdiv_rn(__fsub_rn(line_at<kShared>(g, 2, cz & 0xFFFFu), p.z), d.z));
+    if (vx && qx <= lim) t = fminf(t, __fdiv_rn(ax, d.x));
+    if (vy && qy <= lim) t = fminf(t, __fdiv_rn(ay, d.y));
+    if (vz && qz <= lim) t = fminf(t, __fdiv_rn(az, d.z));
     return fmaxf(t, kVoidAdvance);
 }
 
@@ -501,7 +509,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
     uint32_t* s_stack = reinterpret_cast<uint32_t*>(smem_raw);   // [kStackLevels][kThreads]
     uint32_t* s_recs = s_stack + kStackLevels * kThreads;           // [n_smem][8]
     const uint32_t n_smem = kMulti ? 0u : a.n_smem;
-    float* s_lines = reinterpret_cast<float*>(s_recs + 8u * n_smem);  // [3][2^D + 1]
+    float* s_lines = reinterpret_cast<float*>(s_recs + 8u * n_smem);  // [3][2^D + 2]
 
     // scene of the lane's ray (uniform for single-scene launches)
     const uint32_t* recs = a.scene.recs;
@@ -525,8 +533,9 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
         const int n = g.n;
         if (threadIdx.x < 3) {
             const unsigned ax = threadIdx.x;
-            s_lines[ax * (n + 1)] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
-            s_lines[ax * (n + 1) + n] = ax == 0 ? bn.x : (ax == 1 ? bn.y : bn.z);
+            s_lines[ax * (n + 2)] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
+            s_lines[ax * (n + 2) + n] = ax == 0 ? bn.x : (ax == 1 ? bn.y : bn.z);
+            s_lines[ax * (n + 2) + n + 1] = __int_as_float(0x7f800000);
         }
         __syncthreads();
         for (int lvl = 0; lvl < D; ++lvl) {
@@ -535,7 +544,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
             for (int w = threadIdx.x; w < 3 * cells; w += blockDim.x) {
                 const int axis = w / cells;
                 const int c = w - axis * cells;
-                float* row = s_lines + axis * (n + 1);
+                float* row = s_lines + axis * (n + 2);
                 row[c * stride + (stride >> 1)] = (row[c * stride] + row[c * stride + stride]) * 0.5f;
             }
             __syncthreads();
@@ -621,9 +630,9 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
                                      cell_closed(pcz, iz, ez);
                 // descent coordinates: on the start box's top face the reference keeps taking the upper half
                 if (use_pre) {
-                    jx = min(ix, static_cast<int>(pcx >> 16) - 1);
-                    jy = min(iy, static_cast<int>(pcy >> 16) - 1);
-                    jz = min(iz, static_cast<int>(pcz >> 16) - 1);
+                    jx = min(ix, cell_hi(pcx) - 1);
+                    jy = min(iy, cell_hi(pcy) - 1);
+                    jz = min(iz, cell_hi(pcz) - 1);
                 } else {
                     jx = min(ix, g.n - 1);
                     jy = min(iy, g.n - 1);
@@ -781,7 +790,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     if (kind == Kind::kGrid) {
         kern = trace_grid_kernel<kFan, kMulti, 2>;
         smem = static_cast<size_t>(kStackLevels) * kThreads * 4u + static_cast<size_t>(a.n_smem) * 32u;
-        if (!kMulti) smem += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 1u) * 4u;
+        if (!kMulti) smem += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
     } else {
         kern = trace_float_kernel<kFan, kMulti>;
         smem = static_cast<size_t>(a.n_smem) * 32u;
@@ -816,7 +825,7 @@ bool pool_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
     if (pool->grid_ok >= 0 && std::memcmp(pool->grid_bmin, bmin, sizeof pool->grid_bmin) == 0 &&
         std::memcmp(pool->grid_bmax, bmax, sizeof pool->grid_bmax) == 0)
         return pool->grid_ok == 1;
-    std::vector<float> lines((static_cast<size_t>(1) << pool->height) + 1);
+    std::vector<float> lines((static_cast<size_t>(1) << pool->height) + 2);
     bool ok = true;
     for (int axis = 0; axis < 3 && ok; ++axis) ok = tsdf::build_grid_lines(bmin[axis], bmax[axis], pool->height, lines.data());
     std::memcpy(pool->grid_bmin, bmin, sizeof pool->grid_bmin);
@@ -981,7 +990,7 @@ namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kNoAllocMaxDevices] = {};
-float g_noalloc_lines[(1 << tsdf::kMaxGridDepth) + 1];  // grid-line check buffer, under g_noalloc_mu
+float g_noalloc_lines[(1 << tsdf::kMaxGridDepth) + 2];  // grid-line check buffer, under g_noalloc_mu
 
 // Same decision as pool_grid_ok, with a static buffer instead of a heap vector.
 bool noalloc_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
