@@ -301,13 +301,9 @@ def run_navi(args) -> None:
         raise SystemExit("bench.py needs a CUDA device")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    dist = None
-    if world > 1:
-        import datetime
+    from navi_b200 import dist_stats
 
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    dist = dist_stats.init_from_env("nccl", dev)
 
     from navi_b200 import tracer
     from navi_b200.fan import build_spherical_ray_directions
@@ -391,14 +387,8 @@ def run_navi(args) -> None:
 
     # gather per-rank [rays, ms, steps_mean] over NCCL; job time = max over ranks
     stats = torch.tensor([float(n * args.steps), my_ms, steps_mean], dtype=torch.float64, device=dev)
-    if dist is not None:
-        gathered = [torch.zeros_like(stats) for _ in range(world)]
-        dist.all_gather(gathered, stats)
-        table = torch.stack(gathered).cpu().numpy()
-    else:
-        table = stats.cpu().numpy()[None, :]
-    total_rays = float(table[:, 0].sum())
-    job_ms = float(table[:, 1].max())
+    table = dist_stats.gather_rank_stats(stats, dist)
+    total_rays, job_ms = dist_stats.job_figures(table)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
