@@ -128,6 +128,34 @@ TSDF_API int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, in
                   float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
                   float max_distance, void* workspace, void* stream);
 
+/* Observation settings of tsdf_cast_fan_observe (the reference's post-processing,
+ * sdfdag_backend.py:366-473, and observation stack, :1518-1525). */
+typedef struct tsdf_observe {
+    int32_t azimuth_bins;        /* fan is azimuth-major: ray = az * elevation_bins + el */
+    int32_t elevation_bins;
+    float structure_band_min;    /* structure-band ratios are 0 unless max > min */
+    float structure_band_max;
+    float proximity_threshold;   /* proximity ratio is 0 unless > 0 */
+    float* observation;          /* device [actors][3][az][el] f32: depth, semantic, valid */
+    float* actor_stats;          /* device [actors][5] f32: min clamped distance, starvation,
+                                    proximity, structure band, forward structure band */
+} tsdf_observe;
+
+/* Device bytes of workspace tsdf_cast_fan_observe needs for n_actors. */
+TSDF_API uint64_t tsdf_observe_workspace_bytes(int64_t n_actors);
+
+/* tsdf_cast_fan plus the reference's post-processing fused into the ray writeback:
+ * distances are clamped to [0, max_distance], depth = clamp(log1p(d) / log1p(max), 0, 1),
+ * valid = isfinite(d); the observation tensor and the per-actor reductions
+ * (_compute_observation_ratios_tensor, sdfdag_backend.py:366-405; min distance :459)
+ * are written on `stream`.  Replaces _postprocess_cast_outputs_tensor
+ * (sdfdag_backend.py:408-473) and the stack at :1518-1525. */
+TSDF_API int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
+                                   const float* fan_dirs, int64_t rays_per_actor, int use_pitch,
+                                   float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,
+                                   float max_distance, const tsdf_observe* observe, void* workspace,
+                                   void* stream);
+
 /* Allocation-free variant of tsdf_cast (no counterpart in the reference): the
  * same cast with no workspace argument, for callers that cannot allocate device
  * memory while they run (a fixed-rate control loop must not stall in cudaMalloc;

@@ -40,6 +40,18 @@ class PoolStats(ctypes.Structure):
     ]
 
 
+class Observe(ctypes.Structure):
+    _fields_ = [
+        ("azimuth_bins", ctypes.c_int32),
+        ("elevation_bins", ctypes.c_int32),
+        ("structure_band_min", c_float),
+        ("structure_band_max", c_float),
+        ("proximity_threshold", c_float),
+        ("observation", c_void_p),
+        ("actor_stats", c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/tsdf.h
 TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_version": (c_int, []),
@@ -57,6 +69,9 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_cast_fan": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                               c_int, c_float, c_void_p, c_void_p]),
     "tsdf_set_option": (c_int, [c_char_p, c_int64, ctypes.POINTER(c_int64)]),
+    "tsdf_observe_workspace_bytes": (c_uint64, [c_int64]),
+    "tsdf_cast_fan_observe": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_int, c_float, ctypes.POINTER(Observe), c_void_p, c_void_p]),
     "tsdf_cast_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                                   c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p]),
 }

@@ -70,7 +70,91 @@ struct TraceArgs {
     int32_t* out_s;
     int32_t* out_steps;
     unsigned int* counter;
+    // observation epilogue (fan launches with kObserve)
+    float* obs;                  // [actors][3][rays_per_actor]: depth, semantic, valid
+    unsigned int* obs_acc;       // [actors][6]: ~min key, NaN flag, saturated, proximity, band, forward band
+    uint32_t el_bins;
+    uint32_t az_bins;
+    uint32_t fwd_half;           // forward sector: azimuth rows [0, fwd_half) and [az - fwd_half, az)
+    float sat_thr;               // float32(max_distance - 1e-3)
+    float band_min, band_max;
+    float prox;
+    float inv_log_denom;         // float32(1 / log1p(max_distance)) (reciprocal in double)
+    int band_on, prox_on;
 };
+
+// Epilogue of a finished ray (kernel.cu:298-308) plus, for kObserve, the reference's
+// post-processing of that ray (sdfdag_backend.py:436-446, :1518-1525) and its share of
+// the per-actor reductions (:366-405, :459).  The float steps are those of the torch ops
+// the reference runs: clamp = min(max(v, lo), hi) with NaN passed through, log1pf, and a
+// multiply by the scalar denominator's reciprocal (how torch divides by a host scalar).
+template <bool kObserve>
+__device__ __forceinline__ void finish_ray(const TraceArgs& a, uint32_t ray, float dist_out, int32_t sem_out,
+                                           int32_t steps)
+{
+    a.out_d[ray] = dist_out;
+    a.out_s[ray] = sem_out;
+    if (a.out_steps) a.out_steps[ray] = steps;
+    if constexpr (kObserve) {
+        const uint32_t R = a.rays_per_actor;
+        const uint32_t actor = ray / R;
+        const uint32_t k = ray - actor * R;
+        const bool valid = isfinite(dist_out);
+        const bool nan = isnan(dist_out);
+        float c = dist_out;
+        if (!nan) {
+            c = (c < 0.0f) ? 0.0f : c;
+            c = (a.max_distance < c) ? a.max_distance : c;
+        }
+        float dep = __fmul_rn(log1pf(c), a.inv_log_denom);
+        if (!isnan(dep)) {
+            dep = (dep < 0.0f) ? 0.0f : dep;
+            dep = (1.0f < dep) ? 1.0f : dep;
+        }
+        float* o = a.obs + static_cast<size_t>(actor) * 3u * R + k;
+        o[0] = dep;
+        o[R] = static_cast<float>(sem_out);
+        o[2u * static_cast<size_t>(R)] = valid ? 1.0f : 0.0f;
+        unsigned int* acc = a.obs_acc + static_cast<size_t>(actor) * 6u;
+        if (nan) {
+            atomicOr(acc + 1, 1u);
+        } else {
+            const unsigned int b = __float_as_uint(c);
+            const unsigned int key = (b >> 31) ? ~b : (b | 0x80000000u);  // order-preserving
+            atomicMax(acc + 0, ~key);
+        }
+        if (c >= a.sat_thr) atomicAdd(acc + 2, 1u);
+        if (a.prox_on && valid && c <= a.prox) atomicAdd(acc + 3, 1u);
+        if (a.band_on && valid && c >= a.band_min && c <= a.band_max) {
+            atomicAdd(acc + 4, 1u);
+            const uint32_t az = k / a.el_bins;
+            const unsigned int fwd = (az < a.fwd_half ? 1u : 0u) + (az + a.fwd_half >= a.az_bins ? 1u : 0u);
+            if (fwd) atomicAdd(acc + 5, fwd);  // a row in both slices is counted twice, as torch.cat does
+        }
+    }
+}
+
+// Per-actor ratios as torch's mean computes them: sum * (float(A) / float(A * N)).
+__global__ void observe_finalize_kernel(const unsigned int* acc, float* stats, uint32_t actors, float f_all,
+                                        float f_fwd, int band_on, int prox_on)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= actors) return;
+    const unsigned int* c = acc + static_cast<size_t>(i) * 6u;
+    float mn;
+    if (c[1]) {
+        mn = __int_as_float(0x7fc00000);
+    } else {
+        const unsigned int key = ~c[0];
+        mn = __uint_as_float((key >> 31) ? (key & 0x7fffffffu) : ~key);
+    }
+    float* o = stats + static_cast<size_t>(i) * 5u;
+    o[0] = mn;
+    o[1] = fminf(fmaxf(__fmul_rn(static_cast<float>(c[2]), f_all), 0.0f), 1.0f);
+    o[2] = prox_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[3]), f_all), 0.0f), 1.0f) : 0.0f;
+    o[3] = band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[4]), f_all), 0.0f), 1.0f) : 0.0f;
+    o[4] = band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[5]), f_fwd), 0.0f), 1.0f) : 0.0f;
+}
 
 __device__ __forceinline__ bool in_closed(const float3 p, const float3 mn, const float3 mx)
 {
@@ -101,7 +185,7 @@ __device__ __forceinline__ float leaf_distance(uint32_t bits)
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
 }
 
-template <bool kFan, bool kMulti>
+template <bool kFan, bool kMulti, bool kObserve = false>
 __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a)
 {
     extern __shared__ __align__(16) uint32_t s_recs[];
@@ -306,17 +390,13 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
         if (step_done) {
             // ---- end of the march step (kernel.cu:297-304) ----
             if (sem != 0 && dist < eps) {
-                a.out_d[ray] = t;
-                a.out_s[ray] = sem;
-                if (a.out_steps) a.out_steps[ray] = step + 1;
+                finish_ray<kObserve>(a, ray, t, sem, step + 1);
                 active = false;
             } else {
                 t = t + dist;
                 ++step;
                 if (t > a.max_distance || step >= a.max_steps) {
-                    a.out_d[ray] = t;
-                    a.out_s[ray] = 0;
-                    if (a.out_steps) a.out_steps[ray] = step;
+                    finish_ray<kObserve>(a, ray, t, 0, step);
                     active = false;
                 }
             }
@@ -501,7 +581,7 @@ __device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3&
     }
 }
 
-template <bool kFan, bool kMulti, int kLevels>
+template <bool kFan, bool kMulti, int kLevels, bool kObserve = false>
 __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
@@ -735,17 +815,13 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
         if (step_done) {
             // ---- end of the march step (kernel.cu:297-304) ----
             if (sem != 0 && dist < eps) {
-                a.out_d[ray] = t;
-                a.out_s[ray] = sem;
-                if (a.out_steps) a.out_steps[ray] = step + 1;
+                finish_ray<kObserve>(a, ray, t, sem, step + 1);
                 active = false;
             } else {
                 t = t + dist;
                 ++step;
                 if (t > a.max_distance || step >= a.max_steps) {
-                    a.out_d[ray] = t;
-                    a.out_s[ray] = 0;
-                    if (a.out_steps) a.out_steps[ray] = step;
+                    finish_ray<kObserve>(a, ray, t, 0, step);
                     active = false;
                 }
             }
@@ -777,7 +853,9 @@ int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, f
 
 enum class Kind { kFloat, kGrid };
 
-template <bool kFan, bool kMulti>
+constexpr size_t kObserveAccOffset = 256;  // per-actor accumulators follow the work counter
+
+template <bool kFan, bool kMulti, bool kObserve = false>
 int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream)
 {
     cudaError_t e = cudaSetDevice(device);
@@ -788,11 +866,11 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     void (*kern)(TraceArgs);
     size_t smem;
     if (kind == Kind::kGrid) {
-        kern = trace_grid_kernel<kFan, kMulti, 2>;
+        kern = trace_grid_kernel<kFan, kMulti, 2, kObserve>;
         smem = static_cast<size_t>(kStackLevels) * kThreads * 4u + static_cast<size_t>(a.n_smem) * 32u;
         if (!kMulti) smem += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
     } else {
-        kern = trace_float_kernel<kFan, kMulti>;
+        kern = trace_float_kernel<kFan, kMulti, kObserve>;
         smem = static_cast<size_t>(a.n_smem) * 32u;
     }
     if (smem > 48u * 1024u) {
@@ -808,7 +886,10 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
     const int blocks = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(sms) * per_sm, need));
     a.counter = static_cast<unsigned int*>(workspace);
-    e = cudaMemsetAsync(workspace, 0, sizeof(unsigned int), stream);
+    const size_t clear = kObserve ? kObserveAccOffset + static_cast<size_t>(a.n_rays / a.rays_per_actor) * 24u
+                                  : sizeof(unsigned int);
+    if (kObserve) a.obs_acc = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + kObserveAccOffset);
+    e = cudaMemsetAsync(workspace, 0, clear, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
     kern<<<blocks, kThreads, smem, stream>>>(a);
     e = cudaGetLastError();
@@ -933,6 +1014,87 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     a.scene = scenes->host[0];
     return launch<true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace,
                               static_cast<cudaStream_t>(stream));
+}
+
+uint64_t tsdf_observe_workspace_bytes(int64_t n_actors)
+{
+    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 24u;
+}
+
+int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
+                          const float* fan_dirs, int64_t rays_per_actor, int use_pitch, float* out_dist,
+                          int32_t* out_sem, int32_t* out_steps, int max_steps, float max_distance,
+                          const tsdf_observe* observe, void* workspace, void* stream)
+{
+    if (!observe) return fail(TSDF_ERR_INVALID, "observe must not be null");
+    if (!scenes || scenes->n <= 0) return fail(TSDF_ERR_INVALID, "scenes must not be null");
+    if (observe->azimuth_bins <= 0 || observe->elevation_bins <= 0 ||
+        static_cast<int64_t>(observe->azimuth_bins) * observe->elevation_bins != rays_per_actor)
+        return fail(TSDF_ERR_INVALID, "azimuth_bins * elevation_bins must equal rays_per_actor");
+    if (n_actors < 0 || rays_per_actor < 0) return fail(TSDF_ERR_INVALID, "sizes must not be negative");
+    if (rays_per_actor > 0 && n_actors > kMaxRays / rays_per_actor)
+        return fail(TSDF_ERR_INVALID, "number of rays must be in [0, 2^31 - 2^24]");
+    const int64_t n_rays = n_actors * rays_per_actor;
+    int rc = common_checks(n_rays, out_dist, out_sem, max_steps, max_distance, workspace);
+    if (rc != TSDF_OK) return rc;
+    if (n_rays == 0) return TSDF_OK;
+    if (!poses || !fan_dirs) return fail(TSDF_ERR_INVALID, "poses and fan_dirs must not be null");
+    if (!observe->observation || !observe->actor_stats)
+        return fail(TSDF_ERR_INVALID, "observation and actor_stats must not be null");
+    if (reinterpret_cast<uintptr_t>(poses) % 16u != 0)
+        return fail(TSDF_ERR_INVALID, "poses must be 16-byte aligned");
+
+    TraceArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.poses = reinterpret_cast<const float4*>(poses);
+    a.fan = fan_dirs;
+    a.rays_per_actor = static_cast<uint32_t>(rays_per_actor);
+    a.use_pitch = use_pitch ? 1 : 0;
+    a.n_rays = static_cast<uint32_t>(n_rays);
+    a.max_steps = max_steps;
+    a.max_distance = max_distance;
+    a.chunk = clamp_chunk();
+    a.out_d = out_dist;
+    a.out_s = out_sem;
+    a.out_steps = out_steps;
+    a.obs = observe->observation;
+    a.az_bins = static_cast<uint32_t>(observe->azimuth_bins);
+    a.el_bins = static_cast<uint32_t>(observe->elevation_bins);
+    a.fwd_half = static_cast<uint32_t>(std::max(1, observe->azimuth_bins / 6));
+    // the reference's scalars are Python floats: thresholds are formed in double, then
+    // rounded to float32 by the tensor op; torch divides by the scalar log1p(max) by
+    // multiplying with its reciprocal formed in double and rounded once to float32
+    a.sat_thr = static_cast<float>(static_cast<double>(max_distance) - 1e-3);
+    a.band_min = observe->structure_band_min;
+    a.band_max = observe->structure_band_max;
+    a.prox = observe->proximity_threshold;
+    a.band_on = observe->structure_band_max > observe->structure_band_min ? 1 : 0;
+    a.prox_on = observe->proximity_threshold > 0.0f ? 1 : 0;
+    a.inv_log_denom = static_cast<float>(1.0 / std::log1p(static_cast<double>(max_distance)));
+    const float fa = static_cast<float>(n_actors);
+    const float f_all = fa / static_cast<float>(n_rays);
+    const float f_fwd = fa / static_cast<float>(n_actors * 2 * static_cast<int64_t>(a.fwd_half) * observe->elevation_bins);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (scenes->n == 1) {
+        a.scene = scenes->host[0];
+        a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
+                                                           static_cast<int64_t>(a.scene.n_recs)));
+        const bool grid = scenes->grid && g_descent.load() == 0;
+        if (!grid) a.scene.depth = -1;
+        rc = launch<true, false, true>(grid ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace, s);
+    } else {
+        a.table = scenes->d_table;
+        a.scene = scenes->host[0];
+        rc = launch<true, true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a,
+                                      scenes->device, workspace, s);
+    }
+    if (rc != TSDF_OK) return rc;
+    const uint32_t actors = static_cast<uint32_t>(n_actors);
+    observe_finalize_kernel<<<(actors + 255u) / 256u, 256, 0, s>>>(a.obs_acc, observe->actor_stats, actors, f_all,
+                                                                   f_fwd, a.band_on, a.prox_on);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "observe finalize launch");
+    return TSDF_OK;
 }
 
 int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)

@@ -35,6 +35,7 @@ __all__ = [
     "cast_rays_ex",
     "make_poses",
     "cast_fan",
+    "cast_fan_observe",
     "pool_for_tensor",
     "workspace",
     "set_option",
@@ -329,6 +330,58 @@ def cast_fan(
         float(max_distance), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
     )
     _native.check(rc, "tsdf_cast_fan")
+
+
+def cast_fan_observe(
+    scenes: SceneSet,
+    poses: torch.Tensor,
+    fan_dirs: torch.Tensor,
+    azimuth_bins: int,
+    elevation_bins: int,
+    out_distances: torch.Tensor,
+    out_semantics: torch.Tensor,
+    observation: torch.Tensor,
+    actor_stats: torch.Tensor,
+    *,
+    max_steps: int,
+    max_distance: float,
+    structure_band_min: float = 1.5,
+    structure_band_max: float = 30.0,
+    proximity_threshold: float = 2.0,
+    use_pitch: bool = False,
+    out_steps: torch.Tensor | None = None,
+) -> None:
+    """cast_fan plus the reference's post-processing in the same kernel.
+
+    observation: [actors, 3, azimuth_bins, elevation_bins] f32 (depth, semantic, valid),
+    as sdfdag_backend.py:1518-1525 stacks it; actor_stats: [actors, 5] f32 (min clamped
+    distance, starvation, proximity, structure band, forward structure band ratios), as
+    _postprocess_cast_outputs_tensor (sdfdag_backend.py:408-473) returns them.
+    """
+    a, r = poses.shape[0], fan_dirs.shape[0]
+    if azimuth_bins * elevation_bins != r:
+        raise RuntimeError("azimuth_bins * elevation_bins must equal the fan size")
+    if observation.dtype != torch.float32 or observation.numel() != 3 * a * r or not observation.is_contiguous():
+        raise RuntimeError("observation must be a contiguous float32 [actors, 3, az, el] tensor")
+    if actor_stats.dtype != torch.float32 or actor_stats.numel() != 5 * a or not actor_stats.is_contiguous():
+        raise RuntimeError("actor_stats must be a contiguous float32 [actors, 5] tensor")
+    for name, t, dt in (("out_distances", out_distances, torch.float32), ("out_semantics", out_semantics, torch.int32)):
+        if t.numel() != a * r or t.dtype != dt or not t.is_contiguous():
+            raise RuntimeError(f"{name} must be a contiguous {dt} tensor of actors x rays entries")
+    if out_steps is not None and (out_steps.numel() != a * r or out_steps.dtype != torch.int32 or not out_steps.is_contiguous()):
+        raise RuntimeError("out_steps must be a contiguous int32 tensor of actors x rays entries")
+    _same_device(scenes.device, poses, fan_dirs, out_distances, out_semantics, observation, actor_stats, out_steps)
+    lib = _native.tsdf_lib()
+    ws = torch.empty(int(lib.tsdf_observe_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
+    ob = _native.Observe(int(azimuth_bins), int(elevation_bins), float(structure_band_min), float(structure_band_max),
+                         float(proximity_threshold), observation.data_ptr(), actor_stats.data_ptr())
+    rc = lib.tsdf_cast_fan_observe(
+        scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
+        1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
+        ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None), int(max_steps), float(max_distance),
+        ctypes.byref(ob), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
+    )
+    _native.check(rc, "tsdf_cast_fan_observe")
 
 
 def hit_epsilon_for(voxel_size: float) -> float:
