@@ -281,7 +281,26 @@ def _time_reference_kernel(cfg, scene_list, pb, fan, args) -> dict | None:
         torch.cuda.synchronize()
         if i >= args.warmup:
             ms.append(s0.elapsed_time(e0))
+    from oracle import postprocess_ref
+
+    band = _band(scene_list)
+    pp = []
+    for i in range(max(3, min(args.steps, 10)) + 1):
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        postprocess_ref.postprocess(out_d.view(origins.shape[0], -1), out_s.view(origins.shape[0], -1),
+                                    az_bins=cfg.azimuth_bins, el_bins=cfg.elevation_bins,
+                                    max_distance=cfg.max_distance, structure_band_min_distance=band[0],
+                                    structure_band_max_distance=band[1], proximity_distance_threshold=2.0)
+        e0.record()
+        torch.cuda.synchronize()
+        if i:
+            pp.append(s0.elapsed_time(e0))
     return {"value": n / (float(np.mean(ms)) / 1e3), "unit": UNIT, "ms_per_step": float(np.mean(ms)),
+            "postprocess_ms": float(np.mean(pp)),
+            "postprocess": "the reference's torch ops after the cast (sdfdag_backend.py:408-473, :1518-1525)",
             "timing": "CUDA events on the legacy default stream around each launch (mean), L2 flushed between",
             "build": "oracle/_ref/libref_trace_eps.so: reference kernel.cu for sm_100a, kHitEpsilon settable"}
 
@@ -382,6 +401,8 @@ def run_navi(args) -> None:
     if len(scene_list) == 1:
         explicit = {"value": n / (np.median(ex_ms) / 1e3), "unit": UNIT, "ms_per_step": float(np.median(ex_ms))}
 
+    observe = None if args.no_e2e else _observe(torch, tracer, args, cfg, sset, poses[0], fan, use_pitch, flush, dev,
+                                                 scene_list)
     e2e = None if args.no_e2e or len(scene_list) != 1 else _e2e(torch, args, cfg, scene_list[0], o_dev, d_dev, flush, dev)
     e2e_fan = None if args.no_e2e else _e2e_fan(torch, tracer, args, cfg, sset, sets[0], fan, use_pitch, flush, dev)
 
@@ -442,6 +463,7 @@ def run_navi(args) -> None:
             "e2e": e2e,
             "e2e_fan": e2e_fan,
             "explicit_rays": explicit,
+            "observe": observe,
             "roofline": roof,
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "per_rank_ms": [float(x) for x in table[:, 1]],
@@ -463,6 +485,44 @@ def _traffic(workload: str):
         return json.loads(p.read_text()).get(workload)
     except ValueError:
         return None
+
+
+def _observe(torch, tracer, args, cfg, sset, poses, fan, use_pitch, flush, dev, scene_list) -> dict:
+    """Cast with the reference's post-processing fused into the kernel (observation [A,3,Az,El]
+    + per-actor ratios).  The reference's own post-processing (eager torch ops after the cast)
+    is timed by the --impl reference arm."""
+    a, r = poses.shape[0], fan.shape[0]
+    az, el = cfg.azimuth_bins, cfg.elevation_bins
+    band = _band(scene_list)
+    od = torch.empty(a * r, device=dev)
+    os_ = torch.empty(a * r, dtype=torch.int32, device=dev)
+    obs = torch.empty((a, 3, az, el), device=dev)
+    st = torch.empty((a, 5), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fused():
+        tracer.cast_fan_observe(sset, poses, fan, az, el, od, os_, obs, st, max_steps=cfg.max_steps,
+                                max_distance=cfg.max_distance, structure_band_min=band[0], structure_band_max=band[1],
+                                proximity_threshold=2.0, use_pitch=use_pitch)
+
+    fused()
+    ms = []
+    for _ in range(max(3, min(args.steps, 10))):
+        flush.zero_()
+        s0 = torch.cuda.Event(enable_timing=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        fused()
+        e0.record(stream)
+        torch.cuda.synchronize(dev)
+        ms.append(s0.elapsed_time(e0))
+    return {"fused_cast_observe_ms": float(np.mean(ms)), "structure_band": list(band), "proximity": 2.0}
+
+
+def _band(scene_list) -> tuple[float, float]:
+    """Structure band of the reference env: [1.5, min(0.6 x extent, 50)] (sdfdag_backend.py:1920-1926)."""
+    ext = float(scene_list[0].bbox_max[0] - scene_list[0].bbox_min[0])
+    return 1.5, max(2.5, min(0.6 * ext, 50.0))
 
 
 def _e2e(torch, args, cfg, cs, o_dev, d_dev, flush, dev) -> dict:

@@ -82,8 +82,10 @@ struct TsdfSceneDev {
     float bmax[3];
     float eps;
     int32_t depth;                   // grid depth D (cells per axis 2^D); -1: float descent
+    float scale[3];                  // 2^D / (bmax - bmin) per axis, float division
+    float pad_;
 };
-static_assert(sizeof(TsdfSceneDev) == 64, "scene record layout");
+static_assert(sizeof(TsdfSceneDev) == 80, "scene record layout");
 
 struct tsdf_scenes {
     int device = 0;
@@ -95,6 +97,15 @@ struct tsdf_scenes {
 };
 
 namespace tsdf {
+// Cells per unit length along each axis, 2^D / (bmax - bmin), each an IEEE float
+// subtraction and division (the same values the device's __fsub_rn / __fdiv_rn give).
+inline void set_grid_scale(TsdfSceneDev& d)
+{
+    for (int a = 0; a < 3; ++a) {
+        const float ext = d.bmax[a] - d.bmin[a];
+        d.scale[a] = d.depth >= 0 ? static_cast<float>(1 << d.depth) / ext : 0.0f;
+    }
+}
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);

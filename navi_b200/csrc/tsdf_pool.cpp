@@ -377,6 +377,7 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
                 ok = ok && tsdf::build_grid_lines(d.bmin[a], d.bmax[a], p->height, &lines[line_off[i] + a * m]);
             if (ok) d.depth = p->height;
         }
+        tsdf::set_grid_scale(d);
         grid = grid && d.depth >= 0;
     }
     sc->grid = grid;

@@ -581,8 +581,57 @@ __device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3&
     }
 }
 
+// Scene of a lane's ray.  Single-scene launches read uniform kernel parameters and
+// the block's shared grid lines; multi-scene launches keep only a pointer into the
+// scene table and re-read fields at their point of use (L1-resident), which keeps the
+// kernel at 64 registers (4 blocks of 256 per SM).
+template <bool kMulti>
+struct SceneAccess;
+
+template <>
+struct SceneAccess<false> {
+    const TsdfSceneDev* s;
+    GridView g;
+    float3 b0_, bn_, sc_;
+    __device__ __forceinline__ const uint32_t* recs() const { return s->recs; }
+    __device__ __forceinline__ const uint64_t* ext() const { return s->ext; }
+    __device__ __forceinline__ uint32_t root() const { return s->root; }
+    __device__ __forceinline__ int depth() const { return s->depth; }
+    __device__ __forceinline__ float eps() const { return s->eps; }
+    __device__ __forceinline__ GridView grid() const { return g; }
+    __device__ __forceinline__ float3 b0() const { return b0_; }
+    __device__ __forceinline__ float3 bn() const { return bn_; }
+    __device__ __forceinline__ float3 scale() const { return sc_; }
+};
+
+template <>
+struct SceneAccess<true> {
+    const TsdfSceneDev* s;
+    __device__ __forceinline__ const uint32_t* recs() const
+    {
+        return reinterpret_cast<const uint32_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&s->recs)));
+    }
+    __device__ __forceinline__ const uint64_t* ext() const
+    {
+        return reinterpret_cast<const uint64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&s->ext)));
+    }
+    __device__ __forceinline__ uint32_t root() const { return __ldg(&s->root); }
+    __device__ __forceinline__ int depth() const { return __ldg(&s->depth); }
+    __device__ __forceinline__ float eps() const { return __ldg(&s->eps); }
+    __device__ __forceinline__ GridView grid() const
+    {
+        GridView g;
+        g.lines = reinterpret_cast<const float*>(__ldg(reinterpret_cast<const unsigned long long*>(&s->lines)));
+        g.n = 1 << depth();
+        return g;
+    }
+    __device__ __forceinline__ float3 b0() const { return make_float3(__ldg(&s->bmin[0]), __ldg(&s->bmin[1]), __ldg(&s->bmin[2])); }
+    __device__ __forceinline__ float3 bn() const { return make_float3(__ldg(&s->bmax[0]), __ldg(&s->bmax[1]), __ldg(&s->bmax[2])); }
+    __device__ __forceinline__ float3 scale() const { return make_float3(__ldg(&s->scale[0]), __ldg(&s->scale[1]), __ldg(&s->scale[2])); }
+};
+
 template <bool kFan, bool kMulti, int kLevels, bool kObserve = false>
-__global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
+__global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -591,26 +640,23 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
     const uint32_t n_smem = kMulti ? 0u : a.n_smem;
     float* s_lines = reinterpret_cast<float*>(s_recs + 8u * n_smem);  // [3][2^D + 2]
 
-    // scene of the lane's ray (uniform for single-scene launches)
-    const uint32_t* recs = a.scene.recs;
-    const uint64_t* ext = a.scene.ext;
-    uint32_t root = a.scene.root;
-    int D = a.scene.depth;
-    float eps = a.scene.eps;
-    float3 b0 = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
-    float3 bn = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
-    GridView g;
-    g.n = 1 << D;
-    g.lines = kShared ? s_lines : a.scene.lines;
-
+    SceneAccess<kMulti> S;
+    S.s = kMulti ? a.table : &a.scene;
     if constexpr (!kMulti) {
+        const float3 b0 = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
+        const float3 bn = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
+        S.b0_ = b0;
+        S.bn_ = bn;
+        S.sc_ = make_float3(a.scene.scale[0], a.scene.scale[1], a.scene.scale[2]);
+        S.g.n = 1 << a.scene.depth;
+        S.g.lines = s_lines;
         if (n_smem) {
-            const uint4* src = reinterpret_cast<const uint4*>(recs);
+            const uint4* src = reinterpret_cast<const uint4*>(a.scene.recs);
             uint4* dst = reinterpret_cast<uint4*>(s_recs);
             for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
         }
         // grid lines by the midpoint rule, level by level
-        const int n = g.n;
+        const int n = S.g.n;
         if (threadIdx.x < 3) {
             const unsigned ax = threadIdx.x;
             s_lines[ax * (n + 2)] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
@@ -618,7 +664,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
             s_lines[ax * (n + 2) + n + 1] = __int_as_float(0x7f800000);
         }
         __syncthreads();
-        for (int lvl = 0; lvl < D; ++lvl) {
+        for (int lvl = 0; lvl < a.scene.depth; ++lvl) {
             const int stride = n >> lvl;
             const int cells = 1 << lvl;
             for (int w = threadIdx.x; w < 3 * cells; w += blockDim.x) {
@@ -630,9 +676,6 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
             __syncthreads();
         }
     }
-    float3 scale = make_float3(__fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.x, b0.x)),
-                               __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.y, b0.y)),
-                               __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.z, b0.z)));
 
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* my_stack = s_stack + threadIdx.x;
@@ -664,28 +707,17 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
             sem = 0;
             step = 0;
             flags = 0;
-            if constexpr (kMulti) {
-                const TsdfSceneDev* sc = a.table + scene;
-                recs = sc->recs;
-                ext = sc->ext;
-                root = sc->root;
-                D = sc->depth;
-                eps = sc->eps;
-                b0 = make_float3(sc->bmin[0], sc->bmin[1], sc->bmin[2]);
-                bn = make_float3(sc->bmax[0], sc->bmax[1], sc->bmax[2]);
-                g.n = 1 << D;
-                g.lines = sc->lines;
-                scale = make_float3(__fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.x, b0.x)),
-                                    __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.y, b0.y)),
-                                    __fdiv_rn(static_cast<float>(g.n), __fsub_rn(bn.z, b0.z)));
-            }
+            if constexpr (kMulti) S.s = a.table + scene;
         }
         if (!__any_sync(kFull, active)) break;
         if (!active) continue;
 
+        const int D = S.depth();
         bool step_done = false;
         if (!(flags & kInDesc)) {
             // ---- start of a march step (kernel.cu:260-294) ----
+            const GridView g = S.grid();
+            const float3 b0 = S.b0(), bn = S.bn(), scale = S.scale();
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
             bool ex, ey, ez;
             const int ix = grid_index<kShared>(g, 0, p.x, b0.x, bn.x, scale.x, ex);
@@ -736,7 +768,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
                     }
                 } else {
                     level = start;
-                    node = use_pre ? pre_rec : root;
+                    node = use_pre ? pre_rec : S.root();
                     if (use_pre) flags |= kSvHigh;
                     else flags &= ~kSvHigh;
                 }
@@ -756,7 +788,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
                 leaf = node & ~tsdf::kSlotLeafBit;
                 is_leaf = true;
             } else if (node & tsdf::kSlotExtBit) {
-                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(ext) +
+                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
                                                    (node & tsdf::kSlotIndexMask)));
                 is_leaf = true;
             } else {
@@ -771,7 +803,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
                 const int sh = D - 1 - level;
                 const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
                 const size_t si = static_cast<size_t>(node) * 8u + oct;
-                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(recs + si);
+                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(S.recs() + si);
                 leaf_level = level + 1;
                 if (slot == tsdf::kSlotVoid) {
                     vcx = pack_cell(jx, D - leaf_level);
@@ -779,7 +811,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
                     vcz = pack_cell(jz, D - leaf_level);
                     flags |= kVoidOk;
                     const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
-                    dist = cell_exit_distance<kShared>(g, p, d, vcx, vcy, vcz);
+                    dist = cell_exit_distance<kShared>(S.grid(), p, d, vcx, vcy, vcz);
                     sem = 0;
                     done = true;
                 } else if (leaf_level >= kMaxDepth) {
@@ -814,7 +846,7 @@ __global__ void __launch_bounds__(kThreads) trace_grid_kernel(const TraceArgs a)
         }
         if (step_done) {
             // ---- end of the march step (kernel.cu:297-304) ----
-            if (sem != 0 && dist < eps) {
+            if (sem != 0 && dist < S.eps()) {
                 finish_ray<kObserve>(a, ray, t, sem, step + 1);
                 active = false;
             } else {
@@ -967,6 +999,7 @@ int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, in
     a.out_steps = out_steps;
     const bool grid = pool_grid_ok(const_cast<tsdf_pool*>(pool), bbox_min, bbox_max);
     a.scene.depth = grid ? pool->height : -1;
+    tsdf::set_grid_scale(a.scene);
     return launch<false, false>(grid ? Kind::kGrid : Kind::kFloat, a, pool->device, workspace,
                                 static_cast<cudaStream_t>(stream));
 }
@@ -1239,6 +1272,7 @@ extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, co
     a.out_steps = out_steps;
     const bool grid = noalloc_grid_ok(const_cast<tsdf_pool*>(pool), bbox_min, bbox_max);
     a.scene.depth = grid ? pool->height : -1;
+    tsdf::set_grid_scale(a.scene);
     return launch<false, false>(grid ? Kind::kGrid : Kind::kFloat, a, pool->device, scratch,
                                 static_cast<cudaStream_t>(stream));
 }
