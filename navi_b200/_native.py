@@ -13,10 +13,12 @@ from pathlib import Path
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
 TSDF_PATH = LIB_DIR / "libnavi_tsdf.so"
 GMDAG_PATH = LIB_DIR / "libnavi_gmdag.so"
+GMDAG_GPU_PATH = LIB_DIR / "libnavi_gmdag_gpu.so"
 
 _lock = threading.Lock()
 _tsdf: ctypes.CDLL | None = None
 _gmdag: ctypes.CDLL | None = None
+_gmdag_gpu: ctypes.CDLL | None = None
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
@@ -90,6 +92,37 @@ GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {
 }
 
 
+class GpuCompileTiming(ctypes.Structure):
+    """gmdag_gpu_timing of include/gmdag.h."""
+
+    _fields_ = [
+        ("upload_ms", ctypes.c_double),
+        ("seed_ms", ctypes.c_double),
+        ("sweep_ms", ctypes.c_double),
+        ("pyramid_ms", ctypes.c_double),
+        ("levels_ms", ctypes.c_double),
+        ("emit_ms", ctypes.c_double),
+        ("visited_blocks", c_uint64),
+        ("unique_internal", c_uint64),
+    ]
+
+
+GMDAG_GPU_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "gmdag_gpu_last_error": (c_char_p, []),
+    "gmdag_gpu_compile_mesh": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int,
+                                       ctypes.POINTER(c_void_p)]),
+    "gmdag_gpu_compute_sdf": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int, c_void_p,
+                                      ctypes.POINTER(c_float), ctypes.POINTER(c_float), ctypes.POINTER(c_float)]),
+    "gmdag_gpu_compile_grid": (c_int, [c_void_p, c_uint32, c_float, c_int, ctypes.POINTER(c_void_p)]),
+    "gmdag_gpu_result_num_words": (c_uint64, [c_void_p]),
+    "gmdag_gpu_result_header": (None, [c_void_p, ctypes.POINTER(c_float), ctypes.POINTER(c_float),
+                                       ctypes.POINTER(c_float)]),
+    "gmdag_gpu_result_copy_words": (None, [c_void_p, c_void_p]),
+    "gmdag_gpu_result_timing": (None, [c_void_p, ctypes.POINTER(GpuCompileTiming)]),
+    "gmdag_gpu_result_free": (None, [c_void_p]),
+}
+
+
 def _bind(lib: ctypes.CDLL, sigs: dict[str, tuple[object, list[object]]]) -> None:
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -126,6 +159,23 @@ def gmdag_lib() -> ctypes.CDLL:
                 _bind(lib, GMDAG_SIGNATURES)
                 _gmdag = lib
     return _gmdag
+
+
+def gmdag_gpu_lib() -> ctypes.CDLL:
+    """The device scene compiler; raises RuntimeError when it is not built or cannot load."""
+    global _gmdag_gpu
+    if _gmdag_gpu is None:
+        with _lock:
+            if _gmdag_gpu is None:
+                if not GMDAG_GPU_PATH.exists():
+                    raise RuntimeError(
+                        f"navi_b200 device scene compiler not found at {GMDAG_GPU_PATH}; "
+                        "run `python -m navi_b200.build`"
+                    )
+                lib = ctypes.CDLL(str(GMDAG_GPU_PATH))
+                _bind(lib, GMDAG_GPU_SIGNATURES)
+                _gmdag_gpu = lib
+    return _gmdag_gpu
 
 
 def last_error() -> str:

@@ -6,6 +6,8 @@
                      (nvcc, -gencode arch=compute_100a,code=sm_100a, static cudart)
 - libnavi_gmdag.so : the host scene compiler (g++, OpenMP, -ffp-contract=off so
                      that its float arithmetic matches the reference compiler's)
+- libnavi_gmdag_gpu.so : the device scene compiler (nvcc sm_100a, -fmad=false,
+                     IEEE division / sqrt; same words as libnavi_gmdag.so)
 
 Both are rebuilt only when a source is newer than the library.
 """
@@ -81,19 +83,38 @@ def build_tsdf(force: bool = False) -> Path:
 def build_gmdag(force: bool = False) -> Path:
     out = LIB / "libnavi_gmdag.so"
     src = CSRC / "gmdag_compiler.cpp"
-    if force or _stale(out, [src]):
+    if force or _stale(out, [src, CSRC / "gmdag_math.h", INCLUDE / "gmdag.h"]):
         LIB.mkdir(parents=True, exist_ok=True)
         tmp = out.with_suffix(".so.tmp")
         _run([
             host_cxx(), "-O2", "-std=c++17", "-fPIC", "-shared", "-fopenmp",
-            "-ffp-contract=off", "-fno-fast-math", str(src), "-o", str(tmp),
+            "-ffp-contract=off", "-fno-fast-math", f"-I{INCLUDE}", str(src), "-o", str(tmp),
+        ])
+        tmp.replace(out)
+    return out
+
+
+def build_gmdag_gpu(force: bool = False) -> Path:
+    """The device scene compiler: IEEE float semantics on both sides (no FMA
+    contraction, correctly rounded division and sqrt, denormals kept), so that its
+    values equal the host compiler's."""
+    out = LIB / "libnavi_gmdag_gpu.so"
+    src = CSRC / "gmdag_gpu.cu"
+    if force or _stale(out, [src, CSRC / "gmdag_math.h", INCLUDE / "gmdag.h"]):
+        LIB.mkdir(parents=True, exist_ok=True)
+        tmp = out.with_suffix(".so.tmp")
+        _run([
+            _nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+            "-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false",
+            "-Xcompiler", "-ffp-contract=off", "-Xcompiler", "-fvisibility=hidden",
+            "-Xlinker", "--exclude-libs,ALL", f"-I{INCLUDE}", str(src), "-o", str(tmp),
         ])
         tmp.replace(out)
     return out
 
 
 def build_all(force: bool = False) -> list[Path]:
-    return [build_tsdf(force), build_gmdag(force)]
+    return [build_tsdf(force), build_gmdag(force), build_gmdag_gpu(force)]
 
 
 if __name__ == "__main__":

@@ -31,6 +31,9 @@
 #include <string>
 #include <unordered_map>
 #include <vector>
+
+#include "gmdag.h"
+#include "gmdag_math.h"
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -47,147 +50,11 @@ struct CompileResult {
     uint32_t resolution;
 };
 
-// compiler.cpp:342-422 — squared distance from p to triangle (v0, v1, v2).
-// The float expressions keep the reference's evaluation order.
-float point_triangle_dist_sq(float px, float py, float pz, const float* v0, const float* v1,
-                             const float* v2)
-{
-    const float dfx = px - v0[0], dfy = py - v0[1], dfz = pz - v0[2];
-    const float e0x = v1[0] - v0[0], e0y = v1[1] - v0[1], e0z = v1[2] - v0[2];
-    const float e1x = v2[0] - v0[0], e1y = v2[1] - v0[1], e1z = v2[2] - v0[2];
-    const float a00 = e0x * e0x + e0y * e0y + e0z * e0z;
-    const float a01 = e0x * e1x + e0y * e1y + e0z * e1z;
-    const float a11 = e1x * e1x + e1y * e1y + e1z * e1z;
-    const float b0 = -(dfx * e0x + dfy * e0y + dfz * e0z);
-    const float b1 = -(dfx * e1x + dfy * e1y + dfz * e1z);
-    const float det = std::fabs(a00 * a11 - a01 * a01);
-    float s = a01 * b1 - a11 * b0;
-    float t = a01 * b0 - a00 * b1;
-
-    auto edge_t = [&]() -> float {  // clamp along e1 from b1
-        if (b1 >= 0) return 0.0f;
-        if (-b1 >= a11) return 1.0f;
-        return -b1 / a11;
-    };
-    auto edge_s = [&]() -> float {  // clamp along e0 from b0
-        if (b0 >= 0) return 0.0f;
-        if (-b0 >= a00) return 1.0f;
-        return -b0 / a00;
-    };
-
-    if (s + t <= det) {
-        if (s < 0) {
-            if (t < 0) {
-                if (b0 < 0) {
-                    t = 0;
-                    s = (-b0 >= a00) ? 1.0f : -b0 / a00;
-                } else {
-                    s = 0;
-                    t = edge_t();
-                }
-            } else {
-                s = 0;
-                t = edge_t();
-            }
-        } else if (t < 0) {
-            t = 0;
-            s = edge_s();
-        } else {
-            const float inv = 1.0f / det;
-            s *= inv;
-            t *= inv;
-        }
-    } else {
-        if (s < 0) {
-            const float tmp0 = a01 + b0;
-            const float tmp1 = a11 + b1;
-            if (tmp1 > tmp0) {
-                const float numer = tmp1 - tmp0;
-                const float denom = a00 - 2.0f * a01 + a11;
-                s = (numer >= denom) ? 1.0f : numer / denom;
-                t = 1 - s;
-            } else {
-                s = 0;
-                if (tmp1 >= 0) t = 0;
-                else if (-b1 >= a11) t = 1;
-                else t = -b1 / a11;
-            }
-        } else if (t < 0) {
-            const float tmp0 = a01 + b1;
-            const float tmp1 = a00 + b0;
-            if (tmp1 > tmp0) {
-                const float numer = tmp1 - tmp0;
-                const float denom = a00 - 2.0f * a01 + a11;
-                t = (numer >= denom) ? 1.0f : numer / denom;
-                s = 1 - t;
-            } else {
-                t = 0;
-                if (tmp1 >= 0) s = 0;
-                else if (-b0 >= a00) s = 1;
-                else s = -b0 / a00;
-            }
-        } else {
-            const float numer = a11 + b1 - a01 - b0;
-            if (numer <= 0) {
-                s = 0;
-                t = 1;
-            } else {
-                const float denom = a00 - 2.0f * a01 + a11;
-                s = (numer >= denom) ? 1.0f : numer / denom;
-                t = 1 - s;
-            }
-        }
-    }
-    const float rx = v0[0] + s * e0x + t * e1x - px;
-    const float ry = v0[1] + s * e0y + t * e1y - py;
-    const float rz = v0[2] + s * e0z + t * e1z - pz;
-    return rx * rx + ry * ry + rz * rz;
-}
-
-// compiler.cpp:424-442 — Godunov upwind update from the three sorted neighbours.
-inline float eikonal_update(float a, float b, float c, float h)
-{
-    if (a > b) std::swap(a, b);
-    if (b > c) std::swap(b, c);
-    if (a > b) std::swap(a, b);
-    float d = a + h;
-    if (d <= b) return d;
-    d = 0.5f * (a + b + std::sqrt(2.0f * h * h - (a - b) * (a - b)));
-    if (d <= c) return d;
-    const float sum = a + b + c;
-    const float sum_sq = a * a + b * b + c * c;
-    const float disc = sum * sum - 3.0f * (sum_sq - h * h);
-    if (disc >= 0.0f) return (sum + std::sqrt(disc)) / 3.0f;
-    return d;
-}
-
-// compiler.cpp:542-560.  Truncating float->half with an unsigned exponent: a biased
-// exponent below 112 (|f| < 2^-15, zero included) wraps and encodes as infinity.
-// The reference behaves this way and the DAG words must match it.
-uint16_t half_from_float_ref(float f)
-{
-    uint32_t i;
-    std::memcpy(&i, &f, sizeof i);
-    const uint32_t s = (i >> 16) & 0x00008000u;
-    const uint32_t e = ((i >> 23) & 0x000000ffu) - (127u - 15u);
-    uint32_t m = i & 0x007fffffu;
-    if (e == 0u) {  // the reference's `e <= 0` on an unsigned value
-        m = (m | 0x00800000u) >> 1;
-        return static_cast<uint16_t>(s | (m >> 13));
-    }
-    if (e == 0xffu - (127u - 15u)) {
-        if (m == 0) return static_cast<uint16_t>(s | 0x7c00u);
-        return static_cast<uint16_t>(s | 0x7c00u | (m >> 13) | 1u);
-    }
-    if (e > 30u) return static_cast<uint16_t>(s | 0x7c00u);
-    return static_cast<uint16_t>(s | (e << 10) | (m >> 13));
-}
-
-uint64_t leaf_word(float dist, uint16_t semantic)
-{
-    return (1ull << 63) | (static_cast<uint64_t>(semantic) << 16) |
-           static_cast<uint64_t>(half_from_float_ref(dist));
-}
+using gmdag::eikonal_update;
+using gmdag::half_from_float_ref;
+using gmdag::leaf_word;
+using gmdag::mesh_bounds;
+using gmdag::point_triangle_dist_sq;
 
 int threads_or_default(int n_threads)
 {
@@ -201,9 +68,8 @@ int threads_or_default(int n_threads)
 
 // ---------------------------------------------------------------- SDF stage
 
-void seed_triangles(std::vector<float>& grid, int N, const float* bmin, float dx, float dy,
-                    float dz, float h, const float* verts, const uint32_t* idx, uint64_t n_tri,
-                    int n_threads)
+void seed_triangles(std::vector<float>& grid, int N, const float* bmin, const gmdag::GridFrame& frame,
+                    const float* verts, const uint32_t* idx, uint64_t n_tri, int n_threads)
 {
     const int T = threads_or_default(n_threads);
 #ifdef _OPENMP
@@ -222,27 +88,18 @@ void seed_triangles(std::vector<float>& grid, int N, const float* bmin, float dx
             const float* v0 = &verts[static_cast<size_t>(idx[3 * tr]) * 3];
             const float* v1 = &verts[static_cast<size_t>(idx[3 * tr + 1]) * 3];
             const float* v2 = &verts[static_cast<size_t>(idx[3 * tr + 2]) * 3];
-            const float lo_x = std::min({v0[0], v1[0], v2[0]}) - h;
-            const float hi_x = std::max({v0[0], v1[0], v2[0]}) + h;
-            const float lo_y = std::min({v0[1], v1[1], v2[1]}) - h;
-            const float hi_y = std::max({v0[1], v1[1], v2[1]}) + h;
-            const float lo_z = std::min({v0[2], v1[2], v2[2]}) - h;
-            const float hi_z = std::max({v0[2], v1[2], v2[2]}) + h;
-            const int x0 = std::max(0, static_cast<int>((lo_x - bmin[0]) / dx));
-            const int x1 = std::min(N - 1, static_cast<int>((hi_x - bmin[0]) / dx));
-            const int y0 = std::max(0, static_cast<int>((lo_y - bmin[1]) / dy));
-            const int y1 = std::min(N - 1, static_cast<int>((hi_y - bmin[1]) / dy));
-            int zs = std::max(0, static_cast<int>((lo_z - bmin[2]) / dz));
-            int ze = std::min(N - 1, static_cast<int>((hi_z - bmin[2]) / dz));
+            const gmdag::VoxelBox vb = gmdag::triangle_voxels(v0, v1, v2, bmin, frame, N);
+            const int x0 = vb.x0, x1 = vb.x1, y0 = vb.y0, y1 = vb.y1;
+            int zs = vb.z0, ze = vb.z1;
             zs = std::max(zs, z_lo);
             ze = std::min(ze, z_hi);
             for (int z = zs; z <= ze; ++z) {
-                const float pz = bmin[2] + z * dz;
+                const float pz = bmin[2] + z * frame.dz;
                 for (int y = y0; y <= y1; ++y) {
-                    const float py = bmin[1] + y * dy;
+                    const float py = bmin[1] + y * frame.dy;
                     float* row = &grid[(static_cast<size_t>(z) * N + y) * N];
                     for (int x = x0; x <= x1; ++x) {
-                        const float px = bmin[0] + x * dx;
+                        const float px = bmin[0] + x * frame.dx;
                         const float d = std::sqrt(point_triangle_dist_sq(px, py, pz, v0, v1, v2));
                         if (d < row[x]) row[x] = d;
                     }
@@ -405,7 +262,7 @@ private:
             const int M = N_ >> L;
             const size_t k = (static_cast<size_t>(z / size) * M + y / size) * M + x / size;
             const float lo = pyr_->mn[L][k], hi = pyr_->mx[L][k];
-            return !(std::fabs(hi - first) > 1e-6f) && !(std::fabs(lo - first) > 1e-6f);
+            return gmdag::uniform_block(lo, hi, first);
         }
         for (int bz = z; bz < z + size && bz < N_; ++bz)
             for (int by = y; by < y + size && by < N_; ++by)
@@ -485,30 +342,6 @@ private:
     }
 };
 
-// compiler.cpp:313-329
-void mesh_bounds(const float* verts, uint64_t n_verts, uint32_t res, float* bmin, float* bmax,
-                 float* voxel)
-{
-    float lo[3] = {std::numeric_limits<float>::max(), std::numeric_limits<float>::max(),
-                   std::numeric_limits<float>::max()};
-    float hi[3] = {std::numeric_limits<float>::lowest(), std::numeric_limits<float>::lowest(),
-                   std::numeric_limits<float>::lowest()};
-    for (uint64_t v = 0; v < n_verts; ++v) {
-        for (int a = 0; a < 3; ++a) {
-            const float c = verts[3 * v + a];
-            if (c < lo[a]) lo[a] = c;
-            if (c > hi[a]) hi[a] = c;
-        }
-    }
-    const float ext = std::max({hi[0] - lo[0], hi[1] - lo[1], hi[2] - lo[2]});
-    *voxel = (ext + 2.0f) / static_cast<float>(res);
-    for (int a = 0; a < 3; ++a) {
-        const float c = (hi[a] + lo[a]) / 2.0f;
-        bmin[a] = c - (ext + 2.0f) / 2.0f;
-        bmax[a] = c + (ext + 2.0f) / 2.0f;
-    }
-}
-
 }  // namespace
 
 extern "C" {
@@ -548,12 +381,9 @@ int gmdag_compile_mesh(const float* verts, uint64_t n_verts, const uint32_t* idx
         const int N = static_cast<int>(resolution);
         // compiler.cpp:446-451
         std::vector<float> grid(static_cast<size_t>(N) * N * N, std::numeric_limits<float>::max());
-        const float dx = (res->bmax[0] - res->bmin[0]) / N;
-        const float dy = (res->bmax[1] - res->bmin[1]) / N;
-        const float dz = (res->bmax[2] - res->bmin[2]) / N;
-        const float h = std::min({dx, dy, dz});
-        seed_triangles(grid, N, res->bmin, dx, dy, dz, h, verts, idx, n_tri, n_threads);
-        fast_sweep(grid, N, h, n_threads);
+        const gmdag::GridFrame frame = gmdag::grid_frame(res->bmin, res->bmax, N);
+        seed_triangles(grid, N, res->bmin, frame, verts, idx, n_tri, n_threads);
+        fast_sweep(grid, N, frame.h, n_threads);
         Pyramid pyr;
         const bool use_pyr = Pyramid::is_pow2(N) && N > 1;
         if (use_pyr) pyr.build(grid, N, n_threads);
@@ -590,12 +420,9 @@ int gmdag_compute_sdf(const float* verts, uint64_t n_verts, const uint32_t* idx,
     const int N = static_cast<int>(resolution);
     mesh_bounds(verts, n_verts, resolution, bmin, bmax, voxel);
     std::vector<float> grid(static_cast<size_t>(N) * N * N, std::numeric_limits<float>::max());
-    const float dx = (bmax[0] - bmin[0]) / N;
-    const float dy = (bmax[1] - bmin[1]) / N;
-    const float dz = (bmax[2] - bmin[2]) / N;
-    const float h = std::min({dx, dy, dz});
-    seed_triangles(grid, N, bmin, dx, dy, dz, h, verts, idx, n_tri, n_threads);
-    fast_sweep(grid, N, h, n_threads);
+    const gmdag::GridFrame frame = gmdag::grid_frame(bmin, bmax, N);
+    seed_triangles(grid, N, bmin, frame, verts, idx, n_tri, n_threads);
+    fast_sweep(grid, N, frame.h, n_threads);
     std::memcpy(out_grid, grid.data(), grid.size() * sizeof(float));
     return 0;
 }

@@ -197,75 +197,108 @@ class CompiledMesh:
     bbox_min: tuple[float, float, float]  # float32 values as compiled
     bbox_max: tuple[float, float, float]
     voxel_size: float
+    timing: dict | None = None  # device compiler: stage times (ms) and block counts
 
 
-def compile_mesh(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0) -> CompiledMesh:
-    """Compile a triangle mesh to DAG words with the native scene compiler."""
-    lib = _native.gmdag_lib()
+def _mesh_arrays(vertices: np.ndarray, triangles: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     v = np.ascontiguousarray(vertices, dtype=np.float32).reshape(-1, 3)
     t = np.ascontiguousarray(triangles, dtype=np.uint32).reshape(-1, 3)
-    handle = ctypes.c_void_p()
-    rc = lib.gmdag_compile_mesh(
-        v.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(v.shape[0]),
-        t.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(t.shape[0]),
-        ctypes.c_uint32(resolution), ctypes.c_int(threads), ctypes.byref(handle),
-    )
-    if rc != 0:
-        raise RuntimeError(f"gmdag compile failed: {lib.gmdag_last_error().decode()}")
+    return v, t
+
+
+def _read_result(lib: ctypes.CDLL, prefix: str, handle: ctypes.c_void_p, resolution: int) -> CompiledMesh:
     try:
-        n = int(lib.gmdag_result_num_words(handle))
+        n = int(getattr(lib, f"{prefix}_result_num_words")(handle))
         words = np.empty(n, dtype=np.uint64)
-        lib.gmdag_result_copy_words(handle, words.ctypes.data_as(ctypes.c_void_p))
+        getattr(lib, f"{prefix}_result_copy_words")(handle, words.ctypes.data_as(ctypes.c_void_p))
         bmin = (ctypes.c_float * 3)()
         bmax = (ctypes.c_float * 3)()
         vox = ctypes.c_float()
-        lib.gmdag_result_header(handle, bmin, bmax, ctypes.byref(vox))
+        getattr(lib, f"{prefix}_result_header")(handle, bmin, bmax, ctypes.byref(vox))
+        timing = None
+        if prefix == "gmdag_gpu":
+            timing = _native.GpuCompileTiming()
+            lib.gmdag_gpu_result_timing(handle, ctypes.byref(timing))
     finally:
-        lib.gmdag_result_free(handle)
+        getattr(lib, f"{prefix}_result_free")(handle)
     return CompiledMesh(
         nodes=words,
         resolution=int(resolution),
         bbox_min=(bmin[0], bmin[1], bmin[2]),
         bbox_max=(bmax[0], bmax[1], bmax[2]),
         voxel_size=float(vox.value),
+        timing=None if timing is None else {name: getattr(timing, name) for name, _ in timing._fields_},
     )
 
 
-def compute_sdf(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0):
+def compile_mesh(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0,
+                 device: int | None = None) -> CompiledMesh:
+    """Compile a triangle mesh to DAG words.
+
+    device=None runs the host compiler (OpenMP, `threads` threads); device=k runs the
+    device compiler on CUDA device k (power-of-two resolutions).  Both give the same
+    words."""
+    v, t = _mesh_arrays(vertices, triangles)
+    handle = ctypes.c_void_p()
+    if device is None:
+        lib, prefix = _native.gmdag_lib(), "gmdag"
+        rc = lib.gmdag_compile_mesh(
+            v.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(v.shape[0]),
+            t.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(t.shape[0]),
+            ctypes.c_uint32(resolution), ctypes.c_int(threads), ctypes.byref(handle),
+        )
+    else:
+        lib, prefix = _native.gmdag_gpu_lib(), "gmdag_gpu"
+        rc = lib.gmdag_gpu_compile_mesh(
+            v.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(v.shape[0]),
+            t.ctypes.data_as(ctypes.c_void_p), ctypes.c_uint64(t.shape[0]),
+            ctypes.c_uint32(resolution), ctypes.c_int(int(device)), ctypes.byref(handle),
+        )
+    if rc != 0:
+        raise RuntimeError(f"gmdag compile failed: {getattr(lib, prefix + '_last_error')().decode()}")
+    return _read_result(lib, prefix, handle, resolution)
+
+
+def compute_sdf(vertices: np.ndarray, triangles: np.ndarray, resolution: int, *, threads: int = 0,
+                device: int | None = None):
     """Stage 2 of the compiler alone: (dense grid [z, y, x] f32, bbox_min, bbox_max, voxel)."""
-    lib = _native.gmdag_lib()
-    v = np.ascontiguousarray(vertices, dtype=np.float32).reshape(-1, 3)
-    t = np.ascontiguousarray(triangles, dtype=np.uint32).reshape(-1, 3)
+    v, t = _mesh_arrays(vertices, triangles)
     grid = np.empty((resolution, resolution, resolution), np.float32)
     bmin = (ctypes.c_float * 3)()
     bmax = (ctypes.c_float * 3)()
     vox = ctypes.c_float()
-    rc = lib.gmdag_compute_sdf(v.ctypes.data_as(ctypes.c_void_p), v.shape[0], t.ctypes.data_as(ctypes.c_void_p),
-                               t.shape[0], resolution, threads, grid.ctypes.data_as(ctypes.c_void_p), bmin, bmax,
-                               ctypes.byref(vox))
+    if device is None:
+        lib, fn, err = _native.gmdag_lib(), "gmdag_compute_sdf", "gmdag_last_error"
+        arg = threads
+    else:
+        lib, fn, err = _native.gmdag_gpu_lib(), "gmdag_gpu_compute_sdf", "gmdag_gpu_last_error"
+        arg = int(device)
+    rc = getattr(lib, fn)(v.ctypes.data_as(ctypes.c_void_p), v.shape[0], t.ctypes.data_as(ctypes.c_void_p),
+                          t.shape[0], resolution, arg, grid.ctypes.data_as(ctypes.c_void_p), bmin, bmax,
+                          ctypes.byref(vox))
     if rc != 0:
-        raise RuntimeError(f"gmdag compute_sdf failed: {lib.gmdag_last_error().decode()}")
+        raise RuntimeError(f"gmdag compute_sdf failed: {getattr(lib, err)().decode()}")
     return grid, tuple(bmin), tuple(bmax), float(vox.value)
 
 
-def compile_grid(grid: np.ndarray, voxel_size: float, *, threads: int = 0) -> np.ndarray:
+def compile_grid(grid: np.ndarray, voxel_size: float, *, threads: int = 0, device: int | None = None) -> np.ndarray:
     """Stage 3 of the compiler alone: DAG words of a dense grid [z, y, x]."""
-    lib = _native.gmdag_lib()
     g = np.ascontiguousarray(grid, dtype=np.float32)
     n = g.shape[0]
     if g.shape != (n, n, n):
         raise RuntimeError("grid must be cubic [res, res, res]")
     handle = ctypes.c_void_p()
-    rc = lib.gmdag_compile_grid(g.ctypes.data_as(ctypes.c_void_p), n, ctypes.c_float(voxel_size), threads,
-                                ctypes.byref(handle))
+    if device is None:
+        lib, prefix = _native.gmdag_lib(), "gmdag"
+        rc = lib.gmdag_compile_grid(g.ctypes.data_as(ctypes.c_void_p), n, ctypes.c_float(voxel_size), threads,
+                                    ctypes.byref(handle))
+    else:
+        lib, prefix = _native.gmdag_gpu_lib(), "gmdag_gpu"
+        rc = lib.gmdag_gpu_compile_grid(g.ctypes.data_as(ctypes.c_void_p), n, ctypes.c_float(voxel_size),
+                                        int(device), ctypes.byref(handle))
     if rc != 0:
-        raise RuntimeError(f"gmdag compile_grid failed: {lib.gmdag_last_error().decode()}")
-    try:
-        words = np.empty(int(lib.gmdag_result_num_words(handle)), dtype=np.uint64)
-        lib.gmdag_result_copy_words(handle, words.ctypes.data_as(ctypes.c_void_p))
-    finally:
-        lib.gmdag_result_free(handle)
-    return words
+        raise RuntimeError(f"gmdag compile_grid failed: {getattr(lib, prefix + '_last_error')().decode()}")
+    return _read_result(lib, prefix, handle, n).nodes
 
 
 def half_from_float_ref(x: float) -> int:

@@ -61,6 +61,24 @@ def _mesh_hash(sc: scenes.Scene, res: int) -> str:
     return h.hexdigest()[:16]
 
 
+def _compile_device(res: int) -> int | None:
+    """CUDA device for the device compiler, or None for the host compiler.
+
+    ``$NAVI_COMPILER`` = ``host`` | ``device`` | ``auto`` (default: the device
+    compiler when a GPU is visible and the resolution is a power of two).  Both
+    compilers give the same words, so the cache is shared."""
+    mode = os.environ.get("NAVI_COMPILER", "auto")
+    if mode == "host" or res & (res - 1):
+        return None
+    import torch
+
+    if not torch.cuda.is_available():
+        if mode == "device":
+            raise RuntimeError("NAVI_COMPILER=device but no CUDA device is visible")
+        return None
+    return torch.cuda.current_device()
+
+
 def compiled_scene(config: int, scene: int = 0, resolution: int | None = None, threads: int = 0) -> CompiledScene:
     cfg = scenes.CONFIGS[config]
     res = resolution or cfg.resolution
@@ -69,7 +87,7 @@ def compiled_scene(config: int, scene: int = 0, resolution: int | None = None, t
     d = cache_dir()
     path = d / f"c{config}_s{scene}_r{res}_{digest}.gmdag"
     if not path.exists():
-        out = gmdag.compile_mesh(mesh.vertices, mesh.triangles, res, threads=threads)
+        out = gmdag.compile_mesh(mesh.vertices, mesh.triangles, res, threads=threads, device=_compile_device(res))
         gmdag.write_gmdag(path, out.nodes, res, out.bbox_min, out.voxel_size)
     asset = gmdag.load_gmdag_asset(path, validate_layout=False)
     return CompiledScene(config, scene, path, asset, mesh)

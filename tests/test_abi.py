@@ -59,10 +59,43 @@ def test_null_arguments_are_rejected_before_any_cuda_call():
     assert b"pool must not be null" in lib.tsdf_last_error()
 
 
+def _declared_gmdag() -> list[str]:
+    text = (ROOT / "include" / "gmdag.h").read_text()
+    return re.findall(r"^GMDAG_API\s+[\w\s\*]+?\b(gmdag_\w+)\s*\(", text, flags=re.M)
+
+
 def test_scene_compiler_library_loads():
     lib = _native.gmdag_lib()
     for name in _native.GMDAG_SIGNATURES:
         assert hasattr(lib, name)
+
+
+def test_scene_compiler_libraries_export_every_declared_symbol():
+    names = _declared_gmdag()
+    host = [n for n in names if not n.startswith("gmdag_gpu_")]
+    dev = [n for n in names if n.startswith("gmdag_gpu_")]
+    assert host and dev
+    assert set(_native.GMDAG_SIGNATURES) == set(host)
+    assert set(_native.GMDAG_GPU_SIGNATURES) == set(dev)
+    lib = _native.gmdag_lib()
+    for name in host:
+        assert hasattr(lib, name), name
+    gpu = _native.gmdag_gpu_lib()  # loads without a GPU: no CUDA call at load time
+    for name in dev:
+        assert hasattr(gpu, name), name
+
+
+def test_device_compiler_validates_before_any_cuda_call():
+    import ctypes
+
+    lib = _native.gmdag_gpu_lib()
+    out = ctypes.c_void_p()
+    assert lib.gmdag_gpu_compile_mesh(None, 0, None, 0, 64, 0, ctypes.byref(out)) == -1
+    assert b"at least one triangle" in lib.gmdag_gpu_last_error()
+    v = (ctypes.c_float * 9)(0, 0, 0, 1, 0, 0, 0, 1, 0)
+    i = (ctypes.c_uint32 * 3)(0, 1, 2)
+    assert lib.gmdag_gpu_compile_mesh(v, 3, i, 1, 48, 0, ctypes.byref(out)) == -1
+    assert b"power of two" in lib.gmdag_gpu_last_error()
 
 
 @pytest.mark.parametrize("path", [_native.TSDF_PATH])

@@ -188,6 +188,32 @@ def test_config2_full_step_matches_oracle(descent):
     assert_equal(fk.cpu().numpy(), ref["steps"], "steps")
 
 
+def test_config4_full_step_matches_oracle():
+    """Full benchmark step of config 4 (16 actors x 262,144 rays, 2048^3 scene compiled on
+    the device, 40M-word pool, pitch U[-30, 30] deg, 512 steps) against the oracle."""
+    cfg = scenes.CONFIGS[4]
+    cs, fan, poses, o, v = _config_rays(4)
+    sset = tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                           [cs.hit_epsilon])
+    n = o.shape[0] * o.shape[1]
+    fd = torch.empty(n, dtype=torch.float32, device=dev())
+    fs = torch.empty(n, dtype=torch.int32, device=dev())
+    fk = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, fd, fs, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                    use_pitch=True, out_steps=fk)
+    torch.cuda.synchronize()
+    ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, o.cpu().numpy(), v.cpu().numpy(), max_steps=cfg.max_steps,
+                  max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+    assert_bits_equal(fd.cpu().numpy(), ref["dist"], "dist")
+    assert_equal(fs.cpu().numpy(), ref["sem"], "sem")
+    assert_equal(fk.cpu().numpy(), ref["steps"], "steps")
+    # eps = 1e-3 voxel = 2.05e-5 lies below the smallest finite leaf distance the compiler
+    # can encode (distances under 2^-15 become +inf halves), so no ray of this config can
+    # register a hit: every ray marches to the horizon or to max_steps.
+    assert not np.any(ref["sem"] != 0)
+    assert (ref["steps"] > 8).mean() > 0.5
+
+
 def test_multiscene_fan_matches_per_scene_oracle(descent):
     """Config-3 style scenes (rods) at 128^3, three scenes resident together, actors assigned at random."""
     cfg = scenes.CONFIGS[3]
