@@ -886,6 +886,7 @@ int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, f
 enum class Kind { kFloat, kGrid };
 
 constexpr size_t kObserveAccOffset = 256;  // per-actor accumulators follow the work counter
+constexpr int64_t kSmemReservedPerBlock = 1024;  // shared memory the driver reserves per resident block
 
 template <bool kFan, bool kMulti, bool kObserve = false>
 int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream)
@@ -896,15 +897,34 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     void (*kern)(TraceArgs);
-    size_t smem;
+    size_t base;  // shared memory besides the staged records
     if (kind == Kind::kGrid) {
         kern = trace_grid_kernel<kFan, kMulti, 2, kObserve>;
-        smem = static_cast<size_t>(kStackLevels) * kThreads * 4u + static_cast<size_t>(a.n_smem) * 32u;
-        if (!kMulti) smem += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
+        base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
+        if (!kMulti) base += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
     } else {
         kern = trace_float_kernel<kFan, kMulti, kObserve>;
-        smem = static_cast<size_t>(a.n_smem) * 32u;
+        base = 0;
     }
+    // Stage no more top records than the register-limited occupancy leaves room for:
+    // a deep grid (2^11 lines per axis) with 1024 records would drop a block per SM.
+    if (a.n_smem > 0) {
+        int sm_bytes = 0, reg_blocks = 0;
+        e = cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        if (base > 48u * 1024u) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(base));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+        }
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&reg_blocks, kern, kThreads, base);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (reg_blocks > 0) {
+            const int64_t per_block = static_cast<int64_t>(sm_bytes) / reg_blocks - kSmemReservedPerBlock;
+            const int64_t fit = (per_block - static_cast<int64_t>(base)) / 32;
+            a.n_smem = static_cast<uint32_t>(std::max<int64_t>(0, std::min<int64_t>(a.n_smem, fit)));
+        }
+    }
+    const size_t smem = base + static_cast<size_t>(a.n_smem) * 32u;
     if (smem > 48u * 1024u) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
