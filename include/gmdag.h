@@ -55,6 +55,67 @@ GMDAG_API void gmdag_result_copy_words(const void* result, uint64_t* dst);
 GMDAG_API void gmdag_result_free(void* result);
 GMDAG_API uint16_t gmdag_half_from_float(float f);
 
+/* ---------------------------------------------------------------- files and layout */
+
+/* Replaces integration/voxel_dag.py:193-259 (load_gmdag_asset: header "<4sIIffffI",
+ * version 1, payload, no trailing bytes) and :29-78 (_validate_gmdag_dag_layout, a
+ * recursive Python walk; here an explicit stack in the same depth-first order, so the
+ * first error reported is the reference's).  Messages, in gmdag_last_error(), are the
+ * reference's texts. */
+typedef enum gmdag_file_status {
+    GMDAG_FILE_OK = 0,
+    GMDAG_FILE_NOT_FOUND = 1,          /* "gmdag asset does not exist: ..." (FileNotFoundError) */
+    GMDAG_FILE_SHORT_HEADER = 2,
+    GMDAG_FILE_BAD_MAGIC = 3,
+    GMDAG_FILE_BAD_VERSION = 4,
+    GMDAG_FILE_BAD_RESOLUTION = 5,
+    GMDAG_FILE_BAD_VOXEL = 6,
+    GMDAG_FILE_BAD_NODE_COUNT = 7,
+    GMDAG_FILE_BAD_BOUNDS = 8,
+    GMDAG_FILE_SHORT_PAYLOAD = 9,
+    GMDAG_FILE_TRAILING_BYTES = 10,
+    GMDAG_FILE_IO_ERROR = 11,
+    GMDAG_FILE_BUFFER_TOO_SMALL = 12,
+    GMDAG_FILE_BAD_LAYOUT = 13
+} gmdag_file_status;
+
+typedef enum gmdag_layout_kind {
+    GMDAG_LAYOUT_OK = 0,
+    GMDAG_LAYOUT_NODE_OUT_OF_RANGE = 1,
+    GMDAG_LAYOUT_CYCLE = 2,
+    GMDAG_LAYOUT_EMPTY_MASK = 3,
+    GMDAG_LAYOUT_TABLE_BEYOND_PAYLOAD = 4,
+    GMDAG_LAYOUT_TABLE_EXCEEDS_PAYLOAD = 5,
+    GMDAG_LAYOUT_CHILD_OUT_OF_RANGE = 6
+} gmdag_layout_kind;
+
+typedef struct gmdag_file_info {
+    char magic[4];
+    uint32_t version;
+    uint32_t resolution;
+    float bbox_min[3];
+    float voxel_size;
+    uint32_t node_count;
+    uint64_t nodes_found;     /* whole payload words present, at most node_count */
+    uint64_t trailing_bytes;  /* bytes after node_count words */
+} gmdag_file_info;
+
+typedef struct gmdag_layout_error {
+    int32_t kind;             /* gmdag_layout_kind */
+    uint32_t reserved;
+    uint64_t node;            /* node the message names */
+    uint64_t value;           /* child table index or child reference, where the message quotes one */
+} gmdag_layout_error;
+
+/* dst == NULL: header and size checks only (info filled as far as parsed).  Otherwise
+ * dst_words >= node_count and the payload is read into dst; validate != 0 also walks
+ * the layout (GMDAG_FILE_BAD_LAYOUT, *layout filled).  Returns a gmdag_file_status. */
+GMDAG_API int gmdag_file_read(const char* path, uint64_t* dst, uint64_t dst_words, int validate,
+                              gmdag_file_info* info, gmdag_layout_error* layout);
+
+/* 0: valid; 1: invalid (*err filled, message in gmdag_last_error()); -1: bad arguments. */
+GMDAG_API int gmdag_validate_layout(const uint64_t* nodes, uint64_t n_nodes, gmdag_layout_error* err);
+
 /* ---------------------------------------------------------------- device compiler */
 
 /* Stage times of a device compile, milliseconds (host wall clock around each stage). */

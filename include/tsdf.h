@@ -41,7 +41,9 @@ typedef enum tsdf_status {
     TSDF_ERR_LAYOUT = -2,      /* DAG words that cannot be traversed */
     TSDF_ERR_CUDA = -3,        /* a CUDA runtime call failed */
     TSDF_ERR_NO_MEMORY = -4,   /* host or device allocation failed */
-    TSDF_ERR_UNSUPPORTED = -5  /* device is not sm_100 */
+    TSDF_ERR_UNSUPPORTED = -5, /* device is not sm_100 */
+    TSDF_ERR_NOT_FOUND = -6,   /* a file that does not exist */
+    TSDF_ERR_FILE = -7         /* a file that cannot be read or is malformed */
 } tsdf_status;
 
 /* Reference constants (kernel.cuh:7-11, kernel.cu:9). */
@@ -93,6 +95,21 @@ TSDF_API int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int 
  * for that copy. */
 TSDF_API int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words, int device,
                                  uint32_t flags, void* stream, tsdf_pool** out_pool);
+
+/* Same, from a .gmdag file: the file-to-device path of sdfdag_backend.py:1893-1905
+ * (load_gmdag_asset, integration/voxel_dag.py:193-259, with its checks and texts;
+ * validate != 0 adds the layout walk of :29-78) in one call.  bbox_min / bbox_max
+ * (may be null) receive the box the reference derives: bmin from the header and
+ * bmin + voxel_size * resolution formed in double, rounded to float. */
+TSDF_API int tsdf_pool_create_from_file(const char* path, int validate, int device, uint32_t flags,
+                                        tsdf_pool** out_pool, float* bbox_min, float* bbox_max);
+
+/* On-disk cache of a re-packed pool (records, out-of-line leaves), so that a scene
+ * loads without re-packing.  The file is this library's own format ("NPOL", version
+ * 1); loading checks every slot against the record and leaf counts and recomputes
+ * the record-graph height, so a damaged file is rejected, not traced. */
+TSDF_API int tsdf_pool_save(const tsdf_pool* pool, const char* path);
+TSDF_API int tsdf_pool_load(const char* path, int device, tsdf_pool** out_pool);
 
 TSDF_API int tsdf_pool_destroy(tsdf_pool* pool);
 TSDF_API int tsdf_pool_stats_get(const tsdf_pool* pool, tsdf_pool_stats* out);

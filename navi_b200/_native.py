@@ -60,6 +60,10 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_last_error": (c_char_p, []),
     "tsdf_pool_create": (c_int, [c_void_p, c_uint64, c_int, c_uint32, ctypes.POINTER(c_void_p)]),
     "tsdf_pool_create_from_device": (c_int, [c_void_p, c_uint64, c_int, c_uint32, c_void_p, ctypes.POINTER(c_void_p)]),
+    "tsdf_pool_create_from_file": (c_int, [c_char_p, c_int, c_int, c_uint32, ctypes.POINTER(c_void_p),
+                                           ctypes.POINTER(c_float), ctypes.POINTER(c_float)]),
+    "tsdf_pool_save": (c_int, [c_void_p, c_char_p]),
+    "tsdf_pool_load": (c_int, [c_char_p, c_int, ctypes.POINTER(c_void_p)]),
     "tsdf_pool_destroy": (c_int, [c_void_p]),
     "tsdf_pool_stats_get": (c_int, [c_void_p, ctypes.POINTER(PoolStats)]),
     "tsdf_workspace_bytes": (c_uint64, []),
@@ -78,6 +82,33 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                   c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p]),
 }
 
+class GmdagFileInfo(ctypes.Structure):
+    """gmdag_file_info of include/gmdag.h."""
+
+    _fields_ = [
+        ("magic", ctypes.c_char * 4),
+        ("version", c_uint32),
+        ("resolution", c_uint32),
+        ("bbox_min", c_float * 3),
+        ("voxel_size", c_float),
+        ("node_count", c_uint32),
+        ("nodes_found", c_uint64),
+        ("trailing_bytes", c_uint64),
+    ]
+
+
+class GmdagLayoutError(ctypes.Structure):
+    """gmdag_layout_error of include/gmdag.h."""
+
+    _fields_ = [("kind", ctypes.c_int32), ("reserved", c_uint32), ("node", c_uint64), ("value", c_uint64)]
+
+
+TSDF_ERR_NOT_FOUND = -6  # tsdf_status of include/tsdf.h
+TSDF_ERR_FILE = -7
+
+GMDAG_FILE_OK = 0
+GMDAG_FILE_NOT_FOUND = 1
+
 GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gmdag_last_error": (c_char_p, []),
     "gmdag_compile_mesh": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int, ctypes.POINTER(c_void_p)]),
@@ -89,6 +120,9 @@ GMDAG_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gmdag_compute_sdf": (c_int, [c_void_p, c_uint64, c_void_p, c_uint64, c_uint32, c_int, c_void_p,
                                   ctypes.POINTER(c_float), ctypes.POINTER(c_float), ctypes.POINTER(c_float)]),
     "gmdag_compile_grid": (c_int, [c_void_p, c_uint32, c_float, c_int, ctypes.POINTER(c_void_p)]),
+    "gmdag_file_read": (c_int, [c_char_p, c_void_p, c_uint64, c_int, ctypes.POINTER(GmdagFileInfo),
+                                ctypes.POINTER(GmdagLayoutError)]),
+    "gmdag_validate_layout": (c_int, [c_void_p, c_uint64, ctypes.POINTER(GmdagLayoutError)]),
 }
 
 

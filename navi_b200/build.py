@@ -66,8 +66,8 @@ def _run(cmd: list[str]) -> None:
 
 def build_tsdf(force: bool = False) -> Path:
     out = LIB / "libnavi_tsdf.so"
-    srcs = [CSRC / "tsdf_trace.cu", CSRC / "tsdf_pool.cpp"]
-    deps = srcs + [CSRC / "tsdf_internal.h", INCLUDE / "tsdf.h"]
+    srcs = [CSRC / "tsdf_trace.cu", CSRC / "tsdf_pool.cpp", CSRC / "gmdag_io.cpp"]
+    deps = srcs + [CSRC / "tsdf_internal.h", CSRC / "gmdag_io.h", INCLUDE / "tsdf.h", INCLUDE / "gmdag.h"]
     if force or _stale(out, deps):
         LIB.mkdir(parents=True, exist_ok=True)
         tmp = out.with_suffix(".so.tmp")
@@ -82,13 +82,13 @@ def build_tsdf(force: bool = False) -> Path:
 
 def build_gmdag(force: bool = False) -> Path:
     out = LIB / "libnavi_gmdag.so"
-    src = CSRC / "gmdag_compiler.cpp"
-    if force or _stale(out, [src, CSRC / "gmdag_math.h", INCLUDE / "gmdag.h"]):
+    srcs = [CSRC / "gmdag_compiler.cpp", CSRC / "gmdag_io.cpp"]
+    if force or _stale(out, srcs + [CSRC / "gmdag_math.h", CSRC / "gmdag_io.h", INCLUDE / "gmdag.h"]):
         LIB.mkdir(parents=True, exist_ok=True)
         tmp = out.with_suffix(".so.tmp")
         _run([
             host_cxx(), "-O2", "-std=c++17", "-fPIC", "-shared", "-fopenmp",
-            "-ffp-contract=off", "-fno-fast-math", f"-I{INCLUDE}", str(src), "-o", str(tmp),
+            "-ffp-contract=off", "-fno-fast-math", f"-I{INCLUDE}", *map(str, srcs), "-o", str(tmp),
         ])
         tmp.replace(out)
     return out

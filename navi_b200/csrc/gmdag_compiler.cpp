@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "gmdag.h"
+#include "gmdag_io.h"
 #include "gmdag_math.h"
 #ifdef _OPENMP
 #include <omp.h>
@@ -481,6 +482,44 @@ void gmdag_result_copy_words(const void* r, uint64_t* dst)
 }
 
 void gmdag_result_free(void* r) { delete static_cast<CompileResult*>(r); }
+
+int gmdag_file_read(const char* path, uint64_t* dst, uint64_t dst_words, int validate, gmdag_file_info* info,
+                    gmdag_layout_error* layout)
+{
+    g_err.clear();
+    gmdag_file_info local{};
+    gmdag_file_info& I = info ? *info : local;
+    if (layout) *layout = gmdag_layout_error{};
+    const int st = gmdag_io::read_file(path, dst, dst_words, &I);
+    if (st != GMDAG_FILE_OK) {
+        g_err = gmdag_io::message(path, st, I);
+        return st;
+    }
+    if (dst && validate) {
+        gmdag_layout_error e{};
+        if (!gmdag_io::validate_layout(dst, I.node_count, &e)) {
+            if (layout) *layout = e;
+            g_err = gmdag_io::layout_message(e);
+            return GMDAG_FILE_BAD_LAYOUT;
+        }
+    }
+    return GMDAG_FILE_OK;
+}
+
+int gmdag_validate_layout(const uint64_t* nodes, uint64_t n_nodes, gmdag_layout_error* err)
+{
+    g_err.clear();
+    if (!nodes && n_nodes) {
+        g_err = "nodes must not be null";
+        return -1;
+    }
+    gmdag_layout_error e{};
+    const bool ok = gmdag_io::validate_layout(nodes, n_nodes, &e);
+    if (err) *err = e;
+    if (ok) return 0;
+    g_err = gmdag_io::layout_message(e);
+    return 1;
+}
 
 // The reference's float->half conversion, exposed for tests.
 uint16_t gmdag_half_from_float(float f) { return half_from_float_ref(f); }

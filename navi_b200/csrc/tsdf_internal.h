@@ -48,6 +48,13 @@ struct HostPool {
 // lines are not strictly increasing or the kernel's one-cell estimate bound does not hold.
 bool build_grid_lines(float lo, float hi, int depth, float* out);
 
+// Record-graph height (hp.height, -1 when cyclic) from record 0.
+void compute_height(HostPool& hp);
+
+// Checks of a record array read from a pool file (slot ranges, root, leaf table) and
+// the recomputed BFS levels and height.
+int check_records(HostPool& hp, std::string& err);
+
 // Re-pack .gmdag words; returns TSDF_OK or an error with `err` set.
 int build_host_pool(const uint64_t* words, uint64_t n, HostPool& out, std::string& err);
 

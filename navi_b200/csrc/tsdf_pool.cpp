@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <deque>
 #include <limits>
@@ -20,6 +21,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "gmdag_io.h"
 #include "tsdf_internal.h"
 
 namespace tsdf {
@@ -43,6 +45,106 @@ int cuda_fail(cudaError_t e, const char* what)
 }
 
 const char* last_error_cstr() { return g_last_error.c_str(); }
+
+// Height of the record graph (longest chain of records from the root), iterative DFS;
+// a back edge means a cycle (height -1), which only the float descent (32-level cap)
+// handles.
+void compute_height(HostPool& hp)
+{
+    const size_t nr = hp.recs.size() / 8;
+    hp.height = 0;
+    if (nr > 0) {
+        std::vector<int32_t> h(nr, 0);
+        std::vector<uint8_t> state(nr, 0);  // 0 new, 1 open, 2 done
+        std::vector<std::pair<uint32_t, int>> st;
+        st.emplace_back(0u, 0);
+        state[0] = 1;
+        bool cyclic = false;
+        while (!st.empty() && !cyclic) {
+            auto& top = st.back();
+            const uint32_t r = top.first;
+            if (top.second == 8) {
+                int32_t best = 0;
+                for (int o = 0; o < 8; ++o) {
+                    const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + o];
+                    if (sl != kSlotVoid && !(sl & (kSlotLeafBit | kSlotExtBit))) best = std::max(best, h[sl]);
+                }
+                h[r] = best + 1;
+                state[r] = 2;
+                st.pop_back();
+                continue;
+            }
+            const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + top.second];
+            ++top.second;
+            if (sl == kSlotVoid || (sl & (kSlotLeafBit | kSlotExtBit))) continue;
+            if (state[sl] == 1) {
+                cyclic = true;
+            } else if (state[sl] == 0) {
+                state[sl] = 1;
+                st.emplace_back(sl, 0);
+            }
+        }
+        hp.height = cyclic ? -1 : h[0];
+    }
+}
+
+// Slot checks and derived figures of a record array read from a pool file: every
+// internal slot names a record, every out-of-line slot a leaf, and the height and BFS
+// levels are recomputed rather than trusted.
+int check_records(HostPool& hp, std::string& err)
+{
+    const uint64_t nr = hp.recs.size() / 8;
+    const uint64_t ne = hp.ext.size();
+    auto slot_ok = [&](uint32_t sl) {
+        if (sl == kSlotVoid || (sl & kSlotLeafBit)) return true;
+        if (sl & kSlotExtBit) return static_cast<uint64_t>(sl & kSlotIndexMask) < ne;
+        return static_cast<uint64_t>(sl) < nr;
+    };
+    if (nr > kMaxRecords || ne > kMaxRecords) {
+        err = "pool file: too many records";
+        return TSDF_ERR_FILE;
+    }
+    // the root is record 0 whenever it is internal (records are numbered in BFS order)
+    const bool root_leaf = (hp.root & (kSlotLeafBit | kSlotExtBit)) != 0;
+    if (hp.root == kSlotVoid || !slot_ok(hp.root) || (!root_leaf && hp.root != 0) || (root_leaf != (nr == 0))) {
+        err = "pool file: root slot out of range";
+        return TSDF_ERR_FILE;
+    }
+    for (uint64_t i = 0; i < hp.recs.size(); ++i)
+        if (!slot_ok(hp.recs[i])) {
+            err = "pool file: slot " + std::to_string(i) + " out of range";
+            return TSDF_ERR_FILE;
+        }
+    for (uint64_t i = 0; i < ne; ++i)
+        if ((hp.ext[i] >> 63) != 1) {
+            err = "pool file: out-of-line entry " + std::to_string(i) + " is not a leaf word";
+            return TSDF_ERR_FILE;
+        }
+    // BFS levels from record 0
+    hp.levels = 0;
+    if (nr > 0 && !(hp.root & (kSlotLeafBit | kSlotExtBit))) {
+        std::vector<uint32_t> level(nr, 0xFFFFFFFFu);
+        std::vector<uint32_t> q;
+        q.push_back(hp.root);
+        level[hp.root] = 0;
+        uint32_t maxl = 0;
+        for (size_t h = 0; h < q.size(); ++h) {
+            const uint32_t r = q[h];
+            maxl = std::max(maxl, level[r]);
+            for (int o = 0; o < 8; ++o) {
+                const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + o];
+                if (sl == kSlotVoid || (sl & (kSlotLeafBit | kSlotExtBit))) continue;
+                if (level[sl] == 0xFFFFFFFFu) {
+                    level[sl] = level[r] + 1;
+                    q.push_back(sl);
+                }
+            }
+        }
+        hp.levels = maxl + 1;
+    }
+    compute_height(hp);
+    return TSDF_OK;
+}
 
 int build_host_pool(const uint64_t* w, uint64_t n, HostPool& hp, std::string& err)
 {
@@ -130,43 +232,7 @@ int build_host_pool(const uint64_t* w, uint64_t n, HostPool& hp, std::string& er
     }
     hp.levels = rec_node.empty() ? 0 : max_level + 1;
 
-    // height of every record (longest chain of records below it), iterative DFS;
-    // a back edge means a cycle, which only the float descent (32-level cap) handles
-    const size_t nr = rec_node.size();
-    hp.height = 0;
-    if (nr > 0) {
-        std::vector<int32_t> h(nr, 0);
-        std::vector<uint8_t> state(nr, 0);  // 0 new, 1 open, 2 done
-        std::vector<std::pair<uint32_t, int>> st;
-        st.emplace_back(0u, 0);
-        state[0] = 1;
-        bool cyclic = false;
-        while (!st.empty() && !cyclic) {
-            auto& top = st.back();
-            const uint32_t r = top.first;
-            if (top.second == 8) {
-                int32_t best = 0;
-                for (int o = 0; o < 8; ++o) {
-                    const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + o];
-                    if (sl != kSlotVoid && !(sl & (kSlotLeafBit | kSlotExtBit))) best = std::max(best, h[sl]);
-                }
-                h[r] = best + 1;
-                state[r] = 2;
-                st.pop_back();
-                continue;
-            }
-            const uint32_t sl = hp.recs[8 * static_cast<size_t>(r) + top.second];
-            ++top.second;
-            if (sl == kSlotVoid || (sl & (kSlotLeafBit | kSlotExtBit))) continue;
-            if (state[sl] == 1) {
-                cyclic = true;
-            } else if (state[sl] == 0) {
-                state[sl] = 1;
-                st.emplace_back(sl, 0);
-            }
-        }
-        hp.height = cyclic ? -1 : h[0];
-    }
+    compute_height(hp);
     return TSDF_OK;
 }
 
@@ -220,24 +286,9 @@ static int check_device(int device)
     return TSDF_OK;
 }
 
-int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, uint32_t flags,
-                     tsdf_pool** out_pool)
+// Device copy of a host pool (records + out-of-line leaves).
+static int upload_pool(const tsdf::HostPool& hp, uint64_t source_words, int device, tsdf_pool** out_pool)
 {
-    (void)flags;
-    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
-    *out_pool = nullptr;
-    if (!host_words && n_words) return fail(TSDF_ERR_INVALID, "words must not be null");
-    int rc = check_device(device);
-    if (rc != TSDF_OK) return rc;
-    tsdf::HostPool hp;
-    std::string err;
-    try {
-        rc = tsdf::build_host_pool(host_words, n_words, hp, err);
-    } catch (const std::bad_alloc&) {
-        return fail(TSDF_ERR_NO_MEMORY, "out of host memory while re-packing the DAG");
-    }
-    if (rc != TSDF_OK) return fail(rc, err);
-
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     auto* pool = new (std::nothrow) tsdf_pool();
@@ -245,7 +296,7 @@ int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, u
     pool->device = device;
     pool->records = hp.recs.size() / 8;
     pool->ext = hp.ext.size();
-    pool->source_words = n_words;
+    pool->source_words = source_words;
     pool->root = hp.root;
     pool->levels = hp.levels;
     pool->height = hp.height;
@@ -277,6 +328,27 @@ int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, u
     return TSDF_OK;
 }
 
+int tsdf_pool_create(const uint64_t* host_words, uint64_t n_words, int device, uint32_t flags,
+                     tsdf_pool** out_pool)
+{
+    (void)flags;
+    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
+    *out_pool = nullptr;
+    if (!host_words && n_words) return fail(TSDF_ERR_INVALID, "words must not be null");
+    int rc = check_device(device);
+    if (rc != TSDF_OK) return rc;
+    tsdf::HostPool hp;
+    std::string err;
+    try {
+        rc = tsdf::build_host_pool(host_words, n_words, hp, err);
+    } catch (const std::bad_alloc&) {
+        return fail(TSDF_ERR_NO_MEMORY, "out of host memory while re-packing the DAG");
+    }
+    if (rc != TSDF_OK) return fail(rc, err);
+
+    return upload_pool(hp, n_words, device, out_pool);
+}
+
 int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words, int device,
                                  uint32_t flags, void* stream, tsdf_pool** out_pool)
 {
@@ -299,6 +371,133 @@ int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words,
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "copying the DAG words to the host");
     return tsdf_pool_create(host.data(), n_words, device, flags, out_pool);
+}
+
+int tsdf_pool_create_from_file(const char* path, int validate, int device, uint32_t flags,
+                               tsdf_pool** out_pool, float* bbox_min, float* bbox_max)
+{
+    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
+    *out_pool = nullptr;
+    if (!path) return fail(TSDF_ERR_INVALID, "path must not be null");
+    int rc = check_device(device);
+    if (rc != TSDF_OK) return rc;
+    gmdag_file_info info{};
+    int st = gmdag_io::read_file(path, nullptr, 0, &info);
+    std::vector<uint64_t> words;
+    if (st == GMDAG_FILE_OK) {
+        try {
+            words.resize(info.node_count);
+        } catch (const std::bad_alloc&) {
+            return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+        }
+        st = gmdag_io::read_file(path, words.data(), words.size(), &info);
+    }
+    if (st != GMDAG_FILE_OK)
+        return fail(st == GMDAG_FILE_NOT_FOUND ? TSDF_ERR_NOT_FOUND : TSDF_ERR_FILE, gmdag_io::message(path, st, info));
+    if (validate) {
+        gmdag_layout_error le{};
+        if (!gmdag_io::validate_layout(words.data(), words.size(), &le))
+            return fail(TSDF_ERR_LAYOUT, gmdag_io::layout_message(le));
+    }
+    // voxel_dag.py:244-250: bbox_max = bmin + voxel * resolution in double
+    for (int a = 0; a < 3; ++a) {
+        if (bbox_min) bbox_min[a] = info.bbox_min[a];
+        if (bbox_max)
+            bbox_max[a] = static_cast<float>(static_cast<double>(info.bbox_min[a]) +
+                                             static_cast<double>(info.voxel_size) * static_cast<double>(info.resolution));
+    }
+    return tsdf_pool_create(words.data(), words.size(), device, flags, out_pool);
+}
+
+namespace {
+
+struct PoolFileHeader {
+    char magic[4];
+    uint32_t version;
+    uint32_t root;
+    uint32_t reserved;
+    uint64_t records;
+    uint64_t ext;
+    uint64_t source_words;
+};
+static_assert(sizeof(PoolFileHeader) == 40, "pool file header layout");
+
+}  // namespace
+
+int tsdf_pool_save(const tsdf_pool* pool, const char* path)
+{
+    if (!pool || !path) return fail(TSDF_ERR_INVALID, "pool and path must not be null");
+    std::vector<uint32_t> recs;
+    std::vector<uint64_t> ext;
+    try {
+        recs.resize(pool->records * 8);
+        ext.resize(pool->ext);
+    } catch (const std::bad_alloc&) {
+        return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaError_t e = cudaSetDevice(pool->device);
+    if (e == cudaSuccess && !recs.empty())
+        e = cudaMemcpy(recs.data(), pool->d_recs, recs.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && !ext.empty())
+        e = cudaMemcpy(ext.data(), pool->d_ext, ext.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "copying the node pool to the host");
+    PoolFileHeader h{};
+    std::memcpy(h.magic, "NPOL", 4);
+    h.version = 1;
+    h.root = pool->root;
+    h.records = pool->records;
+    h.ext = pool->ext;
+    h.source_words = pool->source_words;
+    const std::string tmp = std::string(path) + ".tmp";
+    FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (!f) return fail(TSDF_ERR_FILE, "cannot write " + tmp);
+    bool ok = std::fwrite(&h, sizeof h, 1, f) == 1;
+    ok = ok && (recs.empty() || std::fwrite(recs.data(), sizeof(uint32_t), recs.size(), f) == recs.size());
+    ok = ok && (ext.empty() || std::fwrite(ext.data(), sizeof(uint64_t), ext.size(), f) == ext.size());
+    ok = (std::fclose(f) == 0) && ok;
+    if (!ok || std::rename(tmp.c_str(), path) != 0) {
+        std::remove(tmp.c_str());
+        return fail(TSDF_ERR_FILE, std::string("cannot write ") + path);
+    }
+    return TSDF_OK;
+}
+
+int tsdf_pool_load(const char* path, int device, tsdf_pool** out_pool)
+{
+    if (!out_pool) return fail(TSDF_ERR_INVALID, "out_pool must not be null");
+    *out_pool = nullptr;
+    if (!path) return fail(TSDF_ERR_INVALID, "path must not be null");
+    int rc = check_device(device);
+    if (rc != TSDF_OK) return rc;
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(TSDF_ERR_NOT_FOUND, std::string("pool file does not exist: ") + path);
+    PoolFileHeader h{};
+    tsdf::HostPool hp;
+    std::string err;
+    bool ok = std::fread(&h, sizeof h, 1, f) == 1 && std::memcmp(h.magic, "NPOL", 4) == 0 && h.version == 1 &&
+              h.records <= tsdf::kMaxRecords && h.ext <= tsdf::kMaxRecords;
+    if (ok) {
+        try {
+            hp.recs.resize(h.records * 8);
+            hp.ext.resize(h.ext);
+        } catch (const std::bad_alloc&) {
+            std::fclose(f);
+            return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
+        }
+        ok = (hp.recs.empty() || std::fread(hp.recs.data(), sizeof(uint32_t), hp.recs.size(), f) == hp.recs.size()) &&
+             (hp.ext.empty() || std::fread(hp.ext.data(), sizeof(uint64_t), hp.ext.size(), f) == hp.ext.size());
+        unsigned char extra;
+        ok = ok && std::fread(&extra, 1, 1, f) == 0;  // nothing after the arrays
+    }
+    std::fclose(f);
+    if (!ok) return fail(TSDF_ERR_FILE, std::string("not a navi pool file (or truncated): ") + path);
+    hp.root = h.root;
+    rc = tsdf::check_records(hp, err);
+    if (rc != TSDF_OK) return fail(rc, err);
+    return upload_pool(hp, h.source_words, device, out_pool);
 }
 
 int tsdf_pool_destroy(tsdf_pool* pool)

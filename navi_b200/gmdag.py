@@ -11,7 +11,8 @@ the child pointer table, whose entries' low 32 bits index child nodes.
 (projects/environment/src/navi_environment/integration/voxel_dag.py:193-259)
 with the same checks and error texts; the layout validator mirrors
 ``_validate_gmdag_dag_layout`` (voxel_dag.py:29-78) but walks the DAG with an
-explicit stack instead of recursion.
+explicit stack instead of recursion.  Both run in C++ (libnavi_gmdag.so,
+``gmdag_file_read`` / ``gmdag_validate_layout`` of include/gmdag.h).
 """
 
 from __future__ import annotations
@@ -51,119 +52,53 @@ class GmDagAsset:
 
 
 def validate_gmdag_layout(nodes: np.ndarray) -> None:
-    """Reject cycles, empty internal masks and out-of-range references reachable from word 0."""
-    nodes = np.asarray(nodes, dtype=np.uint64)
-    node_count = int(nodes.shape[0])
-    state = np.zeros(node_count, dtype=np.uint8)  # 0 new, 1 on stack, 2 done
-    if node_count == 0:
-        msg = "Invalid gmdag DAG layout: node index out of range: 0"
-        raise RuntimeError(msg)
-    # each stack entry: (node index, next child offset)
-    stack: list[list[int]] = [[0, 0]]
-    state[0] = 1
-    while stack:
-        top = stack[-1]
-        node_index = top[0]
-        word = int(nodes[node_index])
-        if (word >> 63) == 1:
-            state[node_index] = 2
-            stack.pop()
-            continue
-        mask = (word >> 55) & 0xFF
-        if mask == 0:
-            msg = f"Invalid gmdag DAG layout: internal node {node_index} has empty child mask"
-            raise RuntimeError(msg)
-        child_base = word & 0xFFFFFFFF
-        child_count = int(mask.bit_count())
-        if top[1] == 0:
-            if child_base >= node_count:
-                msg = (
-                    "Invalid gmdag DAG layout: child pointer table starts beyond payload "
-                    f"at index {child_base}"
-                )
-                raise RuntimeError(msg)
-            if child_base + child_count > node_count:
-                msg = (
-                    "Invalid gmdag DAG layout: child pointer table exceeds payload bounds "
-                    f"for node {node_index}"
-                )
-                raise RuntimeError(msg)
-        if top[1] >= child_count:
-            state[node_index] = 2
-            stack.pop()
-            continue
-        child_index = int(nodes[child_base + top[1]])
-        top[1] += 1
-        if child_index < 0 or child_index >= node_count:
-            msg = (
-                "Invalid gmdag DAG layout: child reference out of range "
-                f"({child_index}) from node {node_index}"
-            )
-            raise RuntimeError(msg)
-        if state[child_index] == 2:
-            continue
-        if state[child_index] == 1:
-            msg = f"Invalid gmdag DAG layout: cycle detected at node index {child_index}"
-            raise RuntimeError(msg)
-        state[child_index] = 1
-        stack.append([child_index, 0])
+    """Reject cycles, empty internal masks and out-of-range references reachable from word 0.
+
+    The walk runs in libnavi_gmdag.so (gmdag_validate_layout): the reference's
+    depth-first order and texts (voxel_dag.py:29-78) without its recursion."""
+    w = np.ascontiguousarray(np.asarray(nodes).view(np.uint64) if np.asarray(nodes).dtype.itemsize == 8
+                             else np.asarray(nodes, dtype=np.uint64))
+    lib = _native.gmdag_lib()
+    err = _native.GmdagLayoutError()
+    rc = lib.gmdag_validate_layout(w.ctypes.data_as(ctypes.c_void_p), w.shape[0], ctypes.byref(err))
+    if rc != 0:
+        raise RuntimeError(lib.gmdag_last_error().decode())
 
 
 def load_gmdag_asset(path: Path | str, *, validate_layout: bool = True) -> GmDagAsset:
-    """Load a ``.gmdag`` binary into metadata plus a contiguous node array."""
+    """Load a ``.gmdag`` binary into metadata plus a contiguous node array.
+
+    Reading and checks run in libnavi_gmdag.so (gmdag_file_read), in the order and
+    with the texts of voxel_dag.py:193-259."""
     path = Path(path).expanduser().resolve()
-    if not path.exists():
-        msg = f"gmdag asset does not exist: {path}"
-        raise FileNotFoundError(msg)
-    with path.open("rb") as handle:
-        header_bytes = handle.read(_HEADER_STRUCT.size)
-        if len(header_bytes) != _HEADER_STRUCT.size:
-            msg = f"Invalid gmdag header in {path}"
-            raise RuntimeError(msg)
-        magic, version, resolution, bmin_x, bmin_y, bmin_z, voxel_size, node_count = (
-            _HEADER_STRUCT.unpack(header_bytes)
-        )
-        if magic != b"GDAG":
-            msg = f"Unsupported gmdag magic in {path}: {magic!r}"
-            raise RuntimeError(msg)
-        if version != 1:
-            msg = f"Unsupported gmdag version in {path}: {version}"
-            raise RuntimeError(msg)
-        if resolution <= 0:
-            msg = f"Invalid gmdag resolution in {path}: {resolution}"
-            raise RuntimeError(msg)
-        if not np.isfinite(voxel_size) or voxel_size <= 0.0:
-            msg = f"Invalid gmdag voxel size in {path}: {voxel_size}"
-            raise RuntimeError(msg)
-        if node_count <= 0:
-            msg = f"Invalid gmdag node count in {path}: {node_count}"
-            raise RuntimeError(msg)
-        if not all(np.isfinite(v) for v in (bmin_x, bmin_y, bmin_z)):
-            msg = f"Invalid gmdag bounds in {path}: non-finite bbox_min values detected"
-            raise RuntimeError(msg)
-        nodes = np.fromfile(handle, dtype=np.uint64, count=node_count)
-        if nodes.shape[0] != node_count:
-            msg = (
-                f"Invalid gmdag node payload in {path}: expected {node_count} nodes, "
-                f"found {nodes.shape[0]}"
-            )
-            raise RuntimeError(msg)
-        if handle.read(1):
-            msg = f"Invalid gmdag payload in {path}: trailing bytes detected"
-            raise RuntimeError(msg)
-    if validate_layout:
-        validate_gmdag_layout(nodes)
-    bbox_min = (float(bmin_x), float(bmin_y), float(bmin_z))
-    extent = float(voxel_size) * int(resolution)  # Python double, voxel_dag.py:244-250
+    lib = _native.gmdag_lib()
+    info = _native.GmdagFileInfo()
+    layout = _native.GmdagLayoutError()
+    raw = str(path).encode()
+    st = lib.gmdag_file_read(raw, None, 0, 0, ctypes.byref(info), ctypes.byref(layout))
+    nodes = None
+    if st == _native.GMDAG_FILE_OK:
+        nodes = np.empty(int(info.node_count), dtype=np.uint64)
+        st = lib.gmdag_file_read(raw, nodes.ctypes.data_as(ctypes.c_void_p), nodes.shape[0],
+                                 1 if validate_layout else 0, ctypes.byref(info), ctypes.byref(layout))
+    if st == _native.GMDAG_FILE_NOT_FOUND:
+        raise FileNotFoundError(lib.gmdag_last_error().decode())
+    if st != _native.GMDAG_FILE_OK:
+        raise RuntimeError(lib.gmdag_last_error().decode())
+    bmin_x, bmin_y, bmin_z = (float(v) for v in info.bbox_min)
+    voxel_size = float(info.voxel_size)
+    resolution = int(info.resolution)
+    bbox_min = (bmin_x, bmin_y, bmin_z)
+    extent = voxel_size * resolution  # Python double, voxel_dag.py:244-250
     bbox_max = (bbox_min[0] + extent, bbox_min[1] + extent, bbox_min[2] + extent)
     return GmDagAsset(
         path=path,
-        version=int(version),
-        resolution=int(resolution),
+        version=int(info.version),
+        resolution=resolution,
         bbox_min=bbox_min,
         bbox_max=bbox_max,
-        voxel_size=float(voxel_size),
-        nodes=np.ascontiguousarray(nodes),
+        voxel_size=voxel_size,
+        nodes=nodes,
     )
 
 

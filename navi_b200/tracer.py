@@ -14,6 +14,7 @@ non-CUDA tensor raises RuntimeError.
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import math
 import threading
 import weakref
@@ -109,6 +110,47 @@ class NodePool:
         )
         return cls(out.value, dev)
 
+    @classmethod
+    def from_file(cls, path: Path | str, device: torch.device | str | int = "cuda", *,
+                  validate_layout: bool = False) -> tuple["NodePool", list[float], list[float]]:
+        """Read a ``.gmdag`` file, re-pack and upload it in one native call
+        (``tsdf_pool_create_from_file``); returns the pool and the float32 box the
+        reference derives (bmin, bmin + voxel * resolution)."""
+        dev = torch.device(device) if not isinstance(device, torch.device) else device
+        if dev.type != "cuda":
+            raise RuntimeError("NodePool requires a CUDA device; CPU is not supported.")
+        idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        lib = _native.tsdf_lib()
+        out = ctypes.c_void_p()
+        bmin = (ctypes.c_float * 3)()
+        bmax = (ctypes.c_float * 3)()
+        raw = str(Path(path).expanduser().resolve()).encode()
+        rc = lib.tsdf_pool_create_from_file(raw, 1 if validate_layout else 0, idx, 0, ctypes.byref(out), bmin, bmax)
+        if rc == _native.TSDF_ERR_NOT_FOUND:
+            raise FileNotFoundError(_native.last_error())
+        _native.check(rc, "tsdf_pool_create_from_file")
+        return cls(out.value, torch.device("cuda", idx)), list(bmin), list(bmax)
+
+    def save(self, path: Path | str) -> Path:
+        """Write the re-packed pool to a cache file (``tsdf_pool_save``)."""
+        path = Path(path)
+        path.parent.mkdir(parents=True, exist_ok=True)
+        _native.check(_native.tsdf_lib().tsdf_pool_save(self._handle, str(path).encode()), "tsdf_pool_save")
+        return path
+
+    @classmethod
+    def load(cls, path: Path | str, device: torch.device | str | int = "cuda") -> "NodePool":
+        """Upload a pool cache file written by :meth:`save` (``tsdf_pool_load``; every slot is
+        checked and the record-graph height recomputed before anything reaches the device)."""
+        dev = torch.device(device) if not isinstance(device, torch.device) else device
+        idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        out = ctypes.c_void_p()
+        rc = _native.tsdf_lib().tsdf_pool_load(str(path).encode(), idx, ctypes.byref(out))
+        if rc == _native.TSDF_ERR_NOT_FOUND:
+            raise FileNotFoundError(_native.last_error())
+        _native.check(rc, "tsdf_pool_load")
+        return cls(out.value, torch.device("cuda", idx))
+
     def close(self) -> None:
         self._finalizer()
 
@@ -141,6 +183,16 @@ def pool_for_tensor(dag_tensor: torch.Tensor) -> NodePool:
             _pool_cache.pop(next(iter(_pool_cache)))
         _pool_cache[key] = (weakref.ref(dag_tensor), ptr, numel, version, pool)
         return pool
+
+
+def register_pool(dag_tensor: torch.Tensor, pool: NodePool) -> None:
+    """Record `pool` as the re-packed form of `dag_tensor` (same words), so the drop-in
+    cast_rays(dag_tensor, ...) uses it until the tensor changes."""
+    with _cache_lock:
+        if len(_pool_cache) >= _POOL_CACHE_LIMIT:
+            _pool_cache.pop(next(iter(_pool_cache)))
+        _pool_cache[id(dag_tensor)] = (weakref.ref(dag_tensor), int(dag_tensor.data_ptr()), int(dag_tensor.numel()),
+                                       int(dag_tensor._version), pool)
 
 
 def _bbox3(values: Sequence[float], name: str) -> ctypes.Array:
@@ -215,13 +267,41 @@ class GmDagScene:
         return self.asset.voxel_size
 
 
-def load_gmdag(path: Path | str, device: torch.device | str = "cuda", *, validate_layout: bool = False) -> GmDagScene:
+def _pool_cache_file(cache_dir: Path, gmdag_path: Path) -> Path:
+    st = gmdag_path.stat()
+    key = hashlib.sha256(f"{gmdag_path}|{st.st_size}|{st.st_mtime_ns}|{st.st_ino}".encode()).hexdigest()[:20]
+    return cache_dir / f"{gmdag_path.stem}_{key}.npool"
+
+
+def load_gmdag(path: Path | str, device: torch.device | str = "cuda", *, validate_layout: bool = False,
+               pool_cache: Path | str | None = None) -> GmDagScene:
     """Load a ``.gmdag`` file, upload its words as an int64 tensor (as sdfdag_backend.py:1896-1900
-    does) and build its node pool on the same device."""
-    asset = load_gmdag_asset(Path(path), validate_layout=validate_layout)
+    does) and build its node pool on the same device.
+
+    With ``pool_cache`` (a directory) the re-packed pool is kept on disk, keyed by the
+    file's path, size, mtime and inode, and later loads skip the re-pack.  The pool is
+    also registered for the returned tensor, so ``torch_sdf.cast_rays(scene.dag_tensor, ...)``
+    does not re-pack it either."""
+    path = Path(path).expanduser().resolve()
+    asset = load_gmdag_asset(path, validate_layout=validate_layout)
     dev = torch.device(device)
     dag = torch.from_numpy(asset.nodes.view(np.int64)).to(device=dev, dtype=torch.int64)
-    pool = NodePool.from_words(asset.nodes, dag.device)
+    pool = None
+    cache_file = None
+    if pool_cache is not None:
+        cache_file = _pool_cache_file(Path(pool_cache), path)
+        if cache_file.exists():
+            try:
+                pool = NodePool.load(cache_file, dag.device)
+            except RuntimeError:
+                pool = None  # unreadable cache entry: rebuild it below
+            if pool is not None and pool.stats["source_words"] != asset.nodes.shape[0]:
+                pool = None
+    if pool is None:
+        pool = NodePool.from_words(asset.nodes, dag.device)
+        if cache_file is not None:
+            pool.save(cache_file)
+    register_pool(dag, pool)
     return GmDagScene(asset=asset, dag_tensor=dag, pool=pool)
 
 

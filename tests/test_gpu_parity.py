@@ -410,3 +410,53 @@ def internal_word_(mask: int, base: int) -> int:
     from tests.kat_cases import internal_word
 
     return internal_word(mask, base)
+
+
+def test_pool_from_file_and_pool_cache(tmp_path):
+    """tsdf_pool_create_from_file and the on-disk pool cache give the pool of from_words
+    (same records, same casts), and a damaged cache file is rejected before upload."""
+    from navi_b200 import gmdag
+
+    cs, fan, poses, o, v = _config_rays(1)
+    cfg = scenes.CONFIGS[1]
+    path = gmdag.write_gmdag(tmp_path / "c1.gmdag", cs.words, cfg.resolution, cs.bbox_min, cs.voxel_size)
+    ref_pool = tracer.NodePool.from_words(cs.words, dev())
+    pool, bmin, bmax = tracer.NodePool.from_file(path, dev(), validate_layout=True)
+    asset = gmdag.load_gmdag_asset(path)
+    assert bmin == [float(np.float32(x)) for x in asset.bbox_min]
+    assert bmax == [float(np.float32(x)) for x in asset.bbox_max]
+    assert pool.stats == ref_pool.stats
+
+    def cast(p):
+        d = torch.empty(o.shape[0] * o.shape[1], device=dev())
+        s = torch.empty(o.shape[0] * o.shape[1], dtype=torch.int32, device=dev())
+        tracer.cast_rays_ex(p, o, v, d, s, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                            bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=cs.hit_epsilon)
+        torch.cuda.synchronize()
+        return d.cpu().numpy(), s.cpu().numpy()
+
+    want = cast(ref_pool)
+    for p in (pool,):
+        got = cast(p)
+        assert_bits_equal(got[0], want[0], "dist")
+        assert_equal(got[1], want[1], "sem")
+    scene = tracer.load_gmdag(path, dev(), pool_cache=tmp_path / "pools")
+    cached = list((tmp_path / "pools").glob("*.npool"))
+    assert len(cached) == 1
+    again = tracer.load_gmdag(path, dev(), pool_cache=tmp_path / "pools")
+    assert again.pool.stats == ref_pool.stats
+    got = cast(again.pool)
+    assert_bits_equal(got[0], want[0], "dist (cached pool)")
+    assert tracer.pool_for_tensor(scene.dag_tensor) is scene.pool
+    raw = bytearray(cached[0].read_bytes())
+    raw[40 + 4 * 3] = 0xFE  # first record, slot 3: an internal index far out of range
+    raw[40 + 4 * 3 + 3] = 0x3F
+    bad = tmp_path / "bad.npool"
+    bad.write_bytes(bytes(raw))
+    with pytest.raises(RuntimeError, match="out of range"):
+        tracer.NodePool.load(bad, dev())
+    bad.write_bytes(bytes(raw[:60]))
+    with pytest.raises(RuntimeError, match="truncated"):
+        tracer.NodePool.load(bad, dev())
+    with pytest.raises(FileNotFoundError):
+        tracer.NodePool.from_file(tmp_path / "missing.gmdag", dev())
