@@ -42,6 +42,7 @@ constexpr int64_t kMaxRays = (1ll << 31) - (1ll << 24);
 
 std::atomic<int64_t> g_smem_records{1024};
 std::atomic<int64_t> g_chunk{8};
+std::atomic<int64_t> g_leaf_run{1};  // extra leaf-cache steps a lane may take in place per loop iteration
 std::atomic<int64_t> g_blocks_per_sm{0};
 std::atomic<int64_t> g_descent{0};  // 0: integer grid where possible, 1: float descent only
 
@@ -66,6 +67,7 @@ struct TraceArgs {
     float max_distance;
     uint32_t n_smem;             // records staged in shared memory
     uint32_t chunk;
+    uint32_t leaf_run;           // leaf-cache steps taken in place after a step (grid kernel)
     float* out_d;
     int32_t* out_s;
     int32_t* out_steps;
@@ -845,17 +847,37 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
             }
         }
         if (step_done) {
-            // ---- end of the march step (kernel.cu:297-304) ----
-            if (sem != 0 && dist < S.eps()) {
-                finish_ray<kObserve>(a, ray, t, sem, step + 1);
-                active = false;
-            } else {
+            // ---- end of the march step (kernel.cu:297-304), then up to leaf_run more steps in
+            // place while the next position stays in the cached leaf cell.  Such a step is a
+            // leaf-cache hit in the reference: a point of the closed leaf box is inside the
+            // domain and not strictly inside the void cell (octree cells have disjoint
+            // interiors), so the tests before the leaf test (kernel.cu:265, :108) fail.
+            const float eps = S.eps();
+            for (uint32_t run = 0;; ++run) {
+                if (sem != 0 && dist < eps) {
+                    finish_ray<kObserve>(a, ray, t, sem, step + 1);
+                    active = false;
+                    break;
+                }
                 t = t + dist;
                 ++step;
                 if (t > a.max_distance || step >= a.max_steps) {
                     finish_ray<kObserve>(a, ray, t, 0, step);
                     active = false;
+                    break;
                 }
+                // multi-scene launches read the lines from global memory, where the run
+                // costs more than it saves (config 3: -9%); single-scene launches only
+                if (kMulti || run >= a.leaf_run || !(flags & kLeafOk)) break;
+                const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
+                const GridView g = S.grid();
+                // inclusive bounds of the leaf cell: its grid lines (kernel.cu:114)
+                if (!(p.x >= line_at<kShared>(g, 0, cell_lo(lcx)) && p.x <= line_at<kShared>(g, 0, cell_hi(lcx)) &&
+                      p.y >= line_at<kShared>(g, 1, cell_lo(lcy)) && p.y <= line_at<kShared>(g, 1, cell_hi(lcy)) &&
+                      p.z >= line_at<kShared>(g, 2, cell_lo(lcz)) && p.z <= line_at<kShared>(g, 2, cell_hi(lcz))))
+                    break;
+                dist = leaf_d;
+                sem = leaf_s;
             }
         }
     }
@@ -1014,6 +1036,7 @@ int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, in
     a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
                                                        static_cast<int64_t>(pool->records)));
     a.chunk = clamp_chunk();
+    a.leaf_run = static_cast<uint32_t>(g_leaf_run.load());
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
@@ -1051,6 +1074,7 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     a.max_steps = max_steps;
     a.max_distance = max_distance;
     a.chunk = clamp_chunk();
+    a.leaf_run = static_cast<uint32_t>(g_leaf_run.load());
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
@@ -1107,6 +1131,7 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
     a.max_steps = max_steps;
     a.max_distance = max_distance;
     a.chunk = clamp_chunk();
+    a.leaf_run = static_cast<uint32_t>(g_leaf_run.load());
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
@@ -1160,6 +1185,9 @@ int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
     } else if (std::strcmp(key, "chunk") == 0) {
         if (value < 1 || value > 1024) return fail(TSDF_ERR_INVALID, "chunk must be in [1, 1024]");
         slot = &g_chunk;
+    } else if (std::strcmp(key, "leaf_run") == 0) {
+        if (value < 0 || value > 4096) return fail(TSDF_ERR_INVALID, "leaf_run must be in [0, 4096]");
+        slot = &g_leaf_run;
     } else if (std::strcmp(key, "descent") == 0) {
         if (value < 0 || value > 1) return fail(TSDF_ERR_INVALID, "descent must be 0 (grid where possible) or 1 (float)");
         slot = &g_descent;
@@ -1287,6 +1315,7 @@ extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, co
     a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
                                                        static_cast<int64_t>(pool->records)));
     a.chunk = clamp_chunk();
+    a.leaf_run = static_cast<uint32_t>(g_leaf_run.load());
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
