@@ -135,11 +135,19 @@ TSDF_API int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const floa
                        const float* bbox_max, const float* hit_epsilon, tsdf_scenes** out);
 TSDF_API int tsdf_scenes_destroy(tsdf_scenes* scenes);
 
+/* Device bytes of workspace tsdf_cast_fan needs for n_actors: the work counter
+ * and, for scene tables of more than one scene, the actor order by scene. */
+TSDF_API uint64_t tsdf_fan_workspace_bytes(int64_t n_actors);
+
 /* Fused fan cast: ray (a, r) starts at pose a's origin with the local fan
  * direction fan_dirs[r] (device, [rays_per_actor][3] f32), pitched about the
  * local x axis when use_pitch != 0, then yaw-rotated as
  * sdfdag_backend.py:1303-1310 does, and is traced in scene poses[a].scene.
- * Outputs are [n_actors * rays_per_actor], actor-major. */
+ * Outputs are [n_actors * rays_per_actor], actor-major.  workspace:
+ * tsdf_fan_workspace_bytes(n_actors) bytes on the scenes' device.  Multi-scene
+ * tables trace the actors grouped by scene (the outputs do not depend on the
+ * order); an actor whose scene index is outside the table is not traced: its
+ * rays get a NaN distance, semantic 0 and 0 steps. */
 TSDF_API int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
                   const float* fan_dirs, int64_t rays_per_actor, int use_pitch,
                   float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,

@@ -66,6 +66,7 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_pool_load": (c_int, [c_char_p, c_int, ctypes.POINTER(c_void_p)]),
     "tsdf_pool_destroy": (c_int, [c_void_p]),
     "tsdf_pool_stats_get": (c_int, [c_void_p, ctypes.POINTER(PoolStats)]),
+    "tsdf_fan_workspace_bytes": (c_uint64, [c_int64]),
     "tsdf_workspace_bytes": (c_uint64, []),
     "tsdf_cast": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                           c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p, c_void_p]),

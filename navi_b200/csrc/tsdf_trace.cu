@@ -68,6 +68,8 @@ struct TraceArgs {
     uint32_t n_smem;             // records staged in shared memory
     uint32_t chunk;
     uint32_t leaf_run;           // leaf-cache steps taken in place after a step (grid kernel)
+    const uint32_t* perm;        // multi-scene fan launches: actors in scene order (or null)
+    uint32_t n_scenes;           // multi-scene fan launches: scene table size
     float* out_d;
     int32_t* out_s;
     int32_t* out_steps;
@@ -84,6 +86,84 @@ struct TraceArgs {
     float inv_log_denom;         // float32(1 / log1p(max_distance)) (reciprocal in double)
     int band_on, prox_on;
 };
+
+// Ray `r`: explicit origin/direction, or fan ray (actor, local direction) with the
+// reference's rotation (sdfdag_backend.py:1303-1310) and the optional pitch.
+template <bool kFan>
+__device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3& o, float3& d, int& scene)
+{
+    if constexpr (kFan) {
+        const uint32_t actor = r / a.rays_per_actor;
+        const uint32_t k = r - actor * a.rays_per_actor;
+        const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
+        const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
+        float bx = __ldg(a.fan + 3 * static_cast<size_t>(k));
+        float by = __ldg(a.fan + 3 * static_cast<size_t>(k) + 1);
+        float bz = __ldg(a.fan + 3 * static_cast<size_t>(k) + 2);
+        if (a.use_pitch) {
+            const float yp = __fsub_rn(__fmul_rn(by, p1.y), __fmul_rn(bz, p1.z));
+            const float zp = __fadd_rn(__fmul_rn(by, p1.z), __fmul_rn(bz, p1.y));
+            by = yp;
+            bz = zp;
+        }
+        d.x = __fadd_rn(__fmul_rn(bx, p0.w), __fmul_rn(bz, p1.x));
+        d.y = by;
+        d.z = __fadd_rn(__fmul_rn(-bx, p1.x), __fmul_rn(bz, p0.w));
+        o = make_float3(p0.x, p0.y, p0.z);
+        scene = __float_as_int(p1.w);
+    } else {
+        const float* po = a.origins + 3 * static_cast<size_t>(r);
+        const float* pd = a.dirs + 3 * static_cast<size_t>(r);
+        o = make_float3(__ldg(po), __ldg(po + 1), __ldg(po + 2));
+        d = make_float3(__ldg(pd), __ldg(pd + 1), __ldg(pd + 2));
+        scene = 0;
+    }
+}
+
+// Work item w -> output ray.  Multi-scene fan launches take actors grouped by scene
+// (perm, written by scene_sort_kernel), so that the warps of a block mostly trace one
+// scene and the SM's L1 holds the hot records and grid lines of fewer scenes; outputs
+// stay actor-major.  The traced values do not depend on the order.
+template <bool kFan, bool kMulti>
+__device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w)
+{
+    if constexpr (kFan && kMulti) {
+        if (a.perm) {
+            const uint32_t slot = w / a.rays_per_actor;
+            return __ldg(a.perm + slot) * a.rays_per_actor + (w - slot * a.rays_per_actor);
+        }
+    }
+    return w;
+}
+
+// Counting sort of the actors by scene index, one block: perm[i] = the i-th actor in
+// scene order (scenes ascending, actors of one scene in arbitrary order; indices outside
+// [0, n_scenes) last).
+__global__ void __launch_bounds__(1024) scene_sort_kernel(const float4* __restrict__ poses, uint32_t n_actors,
+                                                          uint32_t n_scenes, uint32_t* __restrict__ perm)
+{
+    extern __shared__ unsigned int bucket[];  // [n_scenes + 1]
+    for (uint32_t i = threadIdx.x; i <= n_scenes; i += blockDim.x) bucket[i] = 0;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < n_actors; i += blockDim.x) {
+        const uint32_t sc = static_cast<uint32_t>(__float_as_int(__ldg(poses + 2 * static_cast<size_t>(i) + 1).w));
+        atomicAdd(&bucket[sc < n_scenes ? sc : n_scenes], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int run = 0;
+        for (uint32_t b = 0; b <= n_scenes; ++b) {
+            const unsigned int c = bucket[b];
+            bucket[b] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < n_actors; i += blockDim.x) {
+        const uint32_t sc = static_cast<uint32_t>(__float_as_int(__ldg(poses + 2 * static_cast<size_t>(i) + 1).w));
+        perm[atomicAdd(&bucket[sc < n_scenes ? sc : n_scenes], 1u)] = i;
+    }
+}
 
 // Epilogue of a finished ray (kernel.cu:298-308) plus, for kObserve, the reference's
 // post-processing of that ray (sdfdag_backend.py:436-446, :1518-1525) and its share of
@@ -253,34 +333,22 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                 }
             }
             if (mine != 0xFFFFFFFFu) {
-                ray = mine;
+                ray = work_ray<kFan, kMulti>(a, mine);
                 active = true;
                 t = 0.f;
                 dist = 0.f;
                 sem = 0;
                 step = 0;
                 flags = 0;
-                if constexpr (kFan) {
-                    const uint32_t actor = mine / a.rays_per_actor;
-                    const uint32_t r = mine - actor * a.rays_per_actor;
-                    const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
-                    const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
-                    float bx = __ldg(a.fan + 3 * static_cast<size_t>(r));
-                    float by = __ldg(a.fan + 3 * static_cast<size_t>(r) + 1);
-                    float bz = __ldg(a.fan + 3 * static_cast<size_t>(r) + 2);
-                    if (a.use_pitch) {
-                        const float yp = __fsub_rn(__fmul_rn(by, p1.y), __fmul_rn(bz, p1.z));
-                        const float zp = __fadd_rn(__fmul_rn(by, p1.z), __fmul_rn(bz, p1.y));
-                        by = yp;
-                        bz = zp;
-                    }
-                    // sdfdag_backend.py:1303-1310, each product rounded on its own
-                    d.x = __fadd_rn(__fmul_rn(bx, p0.w), __fmul_rn(bz, p1.x));
-                    d.y = by;
-                    d.z = __fadd_rn(__fmul_rn(-bx, p1.x), __fmul_rn(bz, p0.w));
-                    o = make_float3(p0.x, p0.y, p0.z);
-                    if constexpr (kMulti) {
-                        const TsdfSceneDev* sc = a.table + __float_as_int(p1.w);
+                int scene = 0;
+                load_ray<kFan>(a, ray, o, d, scene);
+                if constexpr (kMulti) {
+                    if (static_cast<uint32_t>(scene) >= a.n_scenes) {
+                        // no such scene: the ray is not traced (NaN distance, semantic 0, 0 steps)
+                        finish_ray<kObserve>(a, ray, __int_as_float(0x7fc00000), 0, 0);
+                        active = false;
+                    } else {
+                        const TsdfSceneDev* sc = a.table + scene;
                         recs = sc->recs;
                         ext = sc->ext;
                         root = sc->root;
@@ -288,11 +356,6 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                         bmx = make_float3(sc->bmax[0], sc->bmax[1], sc->bmax[2]);
                         eps = sc->eps;
                     }
-                } else {
-                    const float* po = a.origins + 3 * static_cast<size_t>(mine);
-                    const float* pd = a.dirs + 3 * static_cast<size_t>(mine);
-                    o = make_float3(__ldg(po), __ldg(po + 1), __ldg(po + 2));
-                    d = make_float3(__ldg(pd), __ldg(pd + 1), __ldg(pd + 2));
                 }
             }
         }
@@ -550,39 +613,6 @@ __device__ __forceinline__ uint32_t claim_ray(uint32_t& q_next, uint32_t& q_end,
     return mine;
 }
 
-// Ray `r`: explicit origin/direction, or fan ray (actor, local direction) with the
-// reference's rotation (sdfdag_backend.py:1303-1310) and the optional pitch.
-template <bool kFan>
-__device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3& o, float3& d, int& scene)
-{
-    if constexpr (kFan) {
-        const uint32_t actor = r / a.rays_per_actor;
-        const uint32_t k = r - actor * a.rays_per_actor;
-        const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
-        const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
-        float bx = __ldg(a.fan + 3 * static_cast<size_t>(k));
-        float by = __ldg(a.fan + 3 * static_cast<size_t>(k) + 1);
-        float bz = __ldg(a.fan + 3 * static_cast<size_t>(k) + 2);
-        if (a.use_pitch) {
-            const float yp = __fsub_rn(__fmul_rn(by, p1.y), __fmul_rn(bz, p1.z));
-            const float zp = __fadd_rn(__fmul_rn(by, p1.z), __fmul_rn(bz, p1.y));
-            by = yp;
-            bz = zp;
-        }
-        d.x = __fadd_rn(__fmul_rn(bx, p0.w), __fmul_rn(bz, p1.x));
-        d.y = by;
-        d.z = __fadd_rn(__fmul_rn(-bx, p1.x), __fmul_rn(bz, p0.w));
-        o = make_float3(p0.x, p0.y, p0.z);
-        scene = __float_as_int(p1.w);
-    } else {
-        const float* po = a.origins + 3 * static_cast<size_t>(r);
-        const float* pd = a.dirs + 3 * static_cast<size_t>(r);
-        o = make_float3(__ldg(po), __ldg(po + 1), __ldg(po + 2));
-        d = make_float3(__ldg(pd), __ldg(pd + 1), __ldg(pd + 2));
-        scene = 0;
-    }
-}
-
 // Scene of a lane's ray.  Single-scene launches read uniform kernel parameters and
 // the block's shared grid lines; multi-scene launches keep only a pointer into the
 // scene table and re-read fields at their point of use (L1-resident), which keeps the
@@ -701,15 +731,23 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
         const uint32_t mine = claim_ray(q_next, q_end, exhausted, active, lane, a.counter, a.chunk, a.n_rays);
         if (mine != 0xFFFFFFFFu) {
             int scene = 0;
-            load_ray<kFan>(a, mine, o, d, scene);
-            ray = mine;
+            ray = work_ray<kFan, kMulti>(a, mine);
+            load_ray<kFan>(a, ray, o, d, scene);
             active = true;
             t = 0.f;
             dist = 0.f;
             sem = 0;
             step = 0;
             flags = 0;
-            if constexpr (kMulti) S.s = a.table + scene;
+            if constexpr (kMulti) {
+                if (static_cast<uint32_t>(scene) >= a.n_scenes) {
+                    // no such scene: the ray is not traced (NaN distance, semantic 0, 0 steps)
+                    finish_ray<kObserve>(a, ray, __int_as_float(0x7fc00000), 0, 0);
+                    active = false;
+                } else {
+                    S.s = a.table + scene;
+                }
+            }
         }
         if (!__any_sync(kFull, active)) break;
         if (!active) continue;
@@ -989,6 +1027,27 @@ bool pool_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
     return ok;
 }
 
+// Multi-scene fan launches: actor order by scene (scene_sort_kernel) into perm_mem
+// (4 bytes per actor of the caller's workspace), on `stream` before the trace.
+constexpr uint32_t kMaxSortedScenes = 8192;  // shared-memory buckets of the sort
+
+int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, void* perm_mem, cudaStream_t stream)
+{
+    a.n_scenes = static_cast<uint32_t>(scenes->n);
+    a.perm = nullptr;
+    if (static_cast<uint32_t>(scenes->n) > kMaxSortedScenes) return TSDF_OK;  // actor order as given
+    cudaError_t e = cudaSetDevice(scenes->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    auto* perm = static_cast<uint32_t*>(perm_mem);
+    const size_t smem = (static_cast<size_t>(scenes->n) + 1) * sizeof(unsigned int);
+    scene_sort_kernel<<<1, 1024, smem, stream>>>(a.poses, static_cast<uint32_t>(n_actors),
+                                                 static_cast<uint32_t>(scenes->n), perm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scene sort launch");
+    a.perm = perm;
+    return TSDF_OK;
+}
+
 uint32_t clamp_chunk()
 {
     const int64_t c = g_chunk.load();
@@ -1089,13 +1148,21 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     }
     a.table = scenes->d_table;
     a.scene = scenes->host[0];
+    rc = sort_by_scene(a, scenes, n_actors, static_cast<char*>(workspace) + kObserveAccOffset,
+                       static_cast<cudaStream_t>(stream));
+    if (rc != TSDF_OK) return rc;
     return launch<true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace,
                               static_cast<cudaStream_t>(stream));
 }
 
+uint64_t tsdf_fan_workspace_bytes(int64_t n_actors)
+{
+    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 4u;
+}
+
 uint64_t tsdf_observe_workspace_bytes(int64_t n_actors)
 {
-    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 24u;
+    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 28u;
 }
 
 int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
@@ -1163,8 +1230,11 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
     } else {
         a.table = scenes->d_table;
         a.scene = scenes->host[0];
-        rc = launch<true, true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a,
-                                      scenes->device, workspace, s);
+        rc = sort_by_scene(a, scenes, n_actors,
+                           static_cast<char*>(workspace) + kObserveAccOffset + static_cast<size_t>(n_actors) * 24u, s);
+        if (rc == TSDF_OK)
+            rc = launch<true, true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a,
+                                          scenes->device, workspace, s);
     }
     if (rc != TSDF_OK) return rc;
     const uint32_t actors = static_cast<uint32_t>(n_actors);

@@ -401,8 +401,8 @@ def cast_fan(
     if out_steps is not None and (out_steps.numel() != a * r or out_steps.dtype != torch.int32 or not out_steps.is_contiguous()):
         raise RuntimeError("out_steps must be a contiguous int32 tensor of actors x rays entries")
     _same_device(scenes.device, poses, fan_dirs, out_distances, out_semantics, out_steps)
-    ws = workspace(scenes.device)
     lib = _native.tsdf_lib()
+    ws = torch.empty(int(lib.tsdf_fan_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
     rc = lib.tsdf_cast_fan(
         scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
         1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),

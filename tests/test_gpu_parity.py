@@ -460,3 +460,32 @@ def test_pool_from_file_and_pool_cache(tmp_path):
         tracer.NodePool.load(bad, dev())
     with pytest.raises(FileNotFoundError):
         tracer.NodePool.from_file(tmp_path / "missing.gmdag", dev())
+
+
+def test_multiscene_actor_with_unknown_scene_is_not_traced(descent):
+    """A pose whose scene index is outside the scene table: its rays get NaN, semantic 0,
+    0 steps; every other actor's rays are traced as usual."""
+    scene_list = [workloads.compiled_scene(3, s, resolution=64) for s in range(2)]
+    pools = [tracer.NodePool.from_words(cs.words, dev()) for cs in scene_list]
+    sset = tracer.SceneSet(pools, [c.bbox_min for c in scene_list], [c.bbox_max for c in scene_list],
+                           [c.hit_epsilon for c in scene_list])
+    pb = workloads.poses_for(3, scene_list, actors=6)
+    sc = pb.scene.copy()
+    sc[2] = 7
+    sc[4] = -1
+    fan = torch.from_numpy(workloads.fan_for(1)).to(dev())
+    poses = tracer.make_poses(torch.from_numpy(pb.position).to(dev()), torch.from_numpy(pb.yaw).to(dev()),
+                              None, torch.from_numpy(sc).to(dev()))
+    n = 6 * fan.shape[0]
+    d = torch.empty(n, device=dev())
+    s = torch.empty(n, dtype=torch.int32, device=dev())
+    k = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, d, s, max_steps=64, max_distance=30.0, out_steps=k)
+    torch.cuda.synchronize()
+    d = d.cpu().numpy().reshape(6, -1)
+    s = s.cpu().numpy().reshape(6, -1)
+    k = k.cpu().numpy().reshape(6, -1)
+    for a in (2, 4):
+        assert np.all(np.isnan(d[a])) and np.all(s[a] == 0) and np.all(k[a] == 0)
+    for a in (0, 1, 3, 5):
+        assert not np.any(np.isnan(d[a])) and np.all(k[a] > 0)
