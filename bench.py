@@ -154,6 +154,13 @@ def _workload(config: int, rank: int, world: int, pose_sets: int):
     return cfg, scene_list, sets, strong
 
 
+def workloads_pose_subset(pb, sel):
+    """The actors `sel` of a pose batch."""
+    from navi_b200 import workloads
+
+    return workloads.PoseBatch(pb.position[sel], pb.yaw[sel], pb.pitch[sel], pb.scene[sel])
+
+
 def _device_poses(torch, tracer, pb, dev):
     pos = torch.from_numpy(pb.position).to(dev)
     yaw = torch.from_numpy(pb.yaw).to(dev)
@@ -245,11 +252,14 @@ def run_reference(args) -> None:
 
 
 def _time_reference_kernel(cfg, scene_list, pb, fan, args) -> dict | None:
-    """The reference's own CUDA kernel (sm_100a build of kernel.cu) on the full explicit-ray step."""
+    """The reference's own CUDA kernel (sm_100a build of kernel.cu) on the full explicit-ray step.
+
+    With several scenes, the reference casts one scene at a time (sdfdag_backend.py:864-887):
+    one launch per scene over that scene's actors, the step time being the sum."""
     try:
         import torch
 
-        if not torch.cuda.is_available() or len(scene_list) != 1:
+        if not torch.cuda.is_available():
             return None
         from oracle import oracle as O
         from navi_b200 import tracer
@@ -258,29 +268,45 @@ def _time_reference_kernel(cfg, scene_list, pb, fan, args) -> dict | None:
     except Exception as exc:  # noqa: BLE001
         return {"unavailable": str(exc)}
     dev = torch.device("cuda", 0)
-    cs = scene_list[0]
-    dag = torch.from_numpy(O.pad_words(cs.words).view(np.int64)).to(dev)
-    poses = _device_poses(torch, tracer, pb, dev)
-    origins, dirs = _eager_dirs(torch, torch.from_numpy(fan).to(dev), poses)
-    n = origins.shape[0] * origins.shape[1]
-    out_d = torch.empty(n, dtype=torch.float32, device=dev)
-    out_s = torch.empty(n, dtype=torch.int32, device=dev)
+    fan_dev = torch.from_numpy(fan).to(dev)
+    groups = []
+    for s, cs in enumerate(scene_list):
+        sel = np.nonzero(pb.scene == s)[0] if len(scene_list) > 1 else np.arange(pb.position.shape[0])
+        if sel.size == 0:
+            continue
+        sub = workloads_pose_subset(pb, sel)
+        poses_s = _device_poses(torch, tracer, sub, dev)
+        o_s, d_s = _eager_dirs(torch, fan_dev, poses_s)
+        n_s = o_s.shape[0] * o_s.shape[1]
+        groups.append((cs, torch.from_numpy(O.pad_words(cs.words).view(np.int64)).to(dev), o_s, d_s,
+                       torch.empty(n_s, dtype=torch.float32, device=dev), torch.empty(n_s, dtype=torch.int32, device=dev)))
+    n = sum(g[2].shape[0] * g[2].shape[1] for g in groups)
     flush = torch.empty(2 * torch.cuda.get_device_properties(dev).L2_cache_size, dtype=torch.uint8, device=dev)
     ms = []
     legacy = torch.cuda.default_stream(dev)
     for i in range(args.warmup + max(3, min(args.steps, 20))):
         flush.zero_()
-        torch.cuda.synchronize()
-        s0 = torch.cuda.Event(enable_timing=True)
-        e0 = torch.cuda.Event(enable_timing=True)
-        s0.record(legacy)
-        kern.cast(dag, origins, dirs, out_d, out_s, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
-                  bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, resolution=cfg.resolution,
-                  hit_epsilon=cs.hit_epsilon)
-        e0.record(legacy)
-        torch.cuda.synchronize()
+        step_ms = 0.0
+        for cs, dag, o_s, d_s, od, osem in groups:
+            torch.cuda.synchronize()
+            s0 = torch.cuda.Event(enable_timing=True)
+            e0 = torch.cuda.Event(enable_timing=True)
+            s0.record(legacy)
+            kern.cast(dag, o_s, d_s, od, osem, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                      bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, resolution=cfg.resolution,
+                      hit_epsilon=cs.hit_epsilon)
+            e0.record(legacy)
+            torch.cuda.synchronize()
+            step_ms += s0.elapsed_time(e0)
         if i >= args.warmup:
-            ms.append(s0.elapsed_time(e0))
+            ms.append(step_ms)
+    if len(groups) != 1:
+        return {"value": n / (float(np.mean(ms)) / 1e3), "unit": UNIT, "ms_per_step": float(np.mean(ms)),
+                "launches_per_step": len(groups),
+                "timing": "CUDA events on the legacy default stream around each per-scene launch, summed per step "
+                          "(mean), L2 flushed between steps",
+                "build": "oracle/_ref/libref_trace_eps.so: reference kernel.cu for sm_100a, kHitEpsilon settable"}
+    _, _, origins, _, out_d, out_s = groups[0]
     from oracle import postprocess_ref
 
     band = _band(scene_list)
