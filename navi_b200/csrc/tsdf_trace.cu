@@ -494,6 +494,7 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
 
 constexpr int kStackLevels = tsdf::kMaxGridDepth;
 constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
+constexpr uint32_t kNeedExit = 64u;      // step ended in the void cell: exit distance still to compute
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
 constexpr int kLvShift = 16;             // 6 bits: level of the node being descended
 
@@ -764,8 +765,7 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
             const int iy = grid_index<kShared>(g, 1, p.y, b0.y, bn.y, scale.y, ey);
             const int iz = grid_index<kShared>(g, 2, p.z, b0.z, bn.z, scale.z, ez);
             if ((flags & kVoidOk) && cell_open(vcx, ix, ex) && cell_open(vcy, iy, ey) && cell_open(vcz, iz, ez)) {
-                dist = cell_exit_distance<kShared>(g, p, d, vcx, vcy, vcz);
-                sem = 0;
+                flags |= kNeedExit;  // exit distance below, with the descents that end in a void cell
                 step_done = true;
             } else if (!(ix >= 0 && iy >= 0 && iz >= 0 && (ix < g.n || (ix == g.n && ex)) &&
                          (iy < g.n || (iy == g.n && ey)) && (iz < g.n || (iz == g.n && ez)))) {
@@ -849,10 +849,7 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
                     vcx = pack_cell(jx, D - leaf_level);
                     vcy = pack_cell(jy, D - leaf_level);
                     vcz = pack_cell(jz, D - leaf_level);
-                    flags |= kVoidOk;
-                    const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
-                    dist = cell_exit_distance<kShared>(S.grid(), p, d, vcx, vcy, vcz);
-                    sem = 0;
+                    flags |= kVoidOk | kNeedExit;
                     done = true;
                 } else if (leaf_level >= kMaxDepth) {
                     done = true;  // cap reached: dist / sem keep their previous values
@@ -883,6 +880,14 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
                 flags = (flags & ~(kInDesc | (31u << kSdShift))) | (static_cast<uint32_t>(leaf_level) << kSdShift);
                 step_done = true;
             }
+        }
+        if (flags & kNeedExit) {
+            // the step ended in the void cell (cached or just found): its exit distance,
+            // computed here once for both kinds of lanes (kernel.cu:54-85, :188)
+            flags &= ~kNeedExit;
+            const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
+            dist = cell_exit_distance<kShared>(S.grid(), p, d, vcx, vcy, vcz);
+            sem = 0;
         }
         if (step_done) {
             // ---- end of the march step (kernel.cu:297-304), then up to leaf_run more steps in
