@@ -195,11 +195,14 @@ TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, cons
                                int max_steps, float max_distance, const float bbox_min[3],
                                const float bbox_max[3], float hit_epsilon, void* stream);
 
-/* Tuning knobs (process-wide): "smem_records" (records staged in shared
- * memory per block, default 1024), "chunk" (rays a warp claims at once,
- * default 8), "blocks_per_sm" (0 = occupancy maximum), "descent" (0 = integer
- * grid descent wherever the DAG allows it, 1 = float descent only; both give
- * the same results).  Returns the old value through *old_value when not NULL. */
+/* Tuning knobs (process-wide): "smem_records" (top records staged in shared
+ * memory per block, default 0: on sm_100 the L1 serves them as fast; capped so
+ * the block keeps its register-limited occupancy), "chunk" (rays a warp claims
+ * at once, default 8), "leaf_run" (leaf-cache steps a single-scene lane takes in
+ * place after a step, default 1), "blocks_per_sm" (0 = occupancy maximum),
+ * "descent" (0 = integer grid descent wherever the DAG allows it, 1 = float
+ * descent only).  No knob changes results.  Returns the old value through
+ * *old_value when not NULL. */
 TSDF_API int tsdf_set_option(const char* key, int64_t value, int64_t* old_value);
 
 #ifdef __cplusplus

@@ -40,7 +40,7 @@ constexpr int kPrefixDepth = 4;          // kernel.cuh:11
 constexpr int kMaxDepth = 32;            // kernel.cu:136
 constexpr int64_t kMaxRays = (1ll << 31) - (1ll << 24);
 
-std::atomic<int64_t> g_smem_records{1024};
+std::atomic<int64_t> g_smem_records{0};  // top records staged per block (the L1 serves them as well on sm_100)
 std::atomic<int64_t> g_chunk{8};
 std::atomic<int64_t> g_leaf_run{1};  // extra leaf-cache steps a lane may take in place per loop iteration
 std::atomic<int64_t> g_blocks_per_sm{0};

@@ -489,3 +489,49 @@ def test_multiscene_actor_with_unknown_scene_is_not_traced(descent):
         assert np.all(np.isnan(d[a])) and np.all(s[a] == 0) and np.all(k[a] == 0)
     for a in (0, 1, 3, 5):
         assert not np.any(np.isnan(d[a])) and np.all(k[a] > 0)
+
+
+@pytest.mark.parametrize("opts", [
+    {"smem_records": 1024}, {"smem_records": 37}, {"leaf_run": 0}, {"leaf_run": 8}, {"chunk": 1},
+    {"chunk": 64}, {"blocks_per_sm": 1}, {"smem_records": 1024, "leaf_run": 3, "chunk": 3, "blocks_per_sm": 2},
+])
+def test_tuning_options_do_not_change_results(opts):
+    """Every knob of tsdf_set_option changes scheduling only: single- and multi-scene fan
+    casts give the default build's bits under each setting."""
+    cfg = scenes.CONFIGS[1]
+    cs, fan, poses, _, _ = _config_rays(1)
+    multi = [workloads.compiled_scene(3, s, resolution=64) for s in range(3)]
+    pb3 = workloads.poses_for(3, multi, actors=24)
+    poses3 = tracer.make_poses(torch.from_numpy(pb3.position).to(dev()), torch.from_numpy(pb3.yaw).to(dev()),
+                               None, torch.from_numpy(pb3.scene).to(dev()))
+    sets = [
+        (tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                         [cs.hit_epsilon]), poses, True),
+        (tracer.SceneSet([tracer.NodePool.from_words(c.words, dev()) for c in multi], [c.bbox_min for c in multi],
+                         [c.bbox_max for c in multi], [c.hit_epsilon for c in multi]), poses3, False),
+    ]
+
+    def run():
+        out = []
+        for sset, p, pitch in sets:
+            n = p.shape[0] * fan.shape[0]
+            d = torch.empty(n, device=dev())
+            s = torch.empty(n, dtype=torch.int32, device=dev())
+            k = torch.empty(n, dtype=torch.int32, device=dev())
+            tracer.cast_fan(sset, p, fan, d, s, max_steps=cfg.max_steps, max_distance=cfg.max_distance,
+                            use_pitch=pitch, out_steps=k)
+            torch.cuda.synchronize()
+            out.append((d.cpu().numpy(), s.cpu().numpy(), k.cpu().numpy()))
+        return out
+
+    want = run()
+    old = {k: tracer.set_option(k, v) for k, v in opts.items()}
+    try:
+        got = run()
+    finally:
+        for k, v in old.items():
+            tracer.set_option(k, v)
+    for (gd, gs, gk), (wd, ws, wk) in zip(got, want):
+        assert_bits_equal(gd, wd, f"dist under {opts}")
+        assert_equal(gs, ws, f"sem under {opts}")
+        assert_equal(gk, wk, f"steps under {opts}")
