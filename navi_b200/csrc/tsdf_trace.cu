@@ -964,7 +964,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     void (*kern)(TraceArgs);
     size_t base;  // shared memory besides the staged records
     if (kind == Kind::kGrid) {
-        kern = trace_grid_kernel<kFan, kMulti, 2, kObserve>;
+        kern = trace_grid_kernel<kFan, kMulti, 3, kObserve>;
         base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
         if (!kMulti) base += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
     } else {
