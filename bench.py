@@ -542,7 +542,7 @@ def _observe(torch, tracer, args, cfg, sset, poses, fan, use_pitch, flush, dev, 
         e0.record(stream)
         torch.cuda.synchronize(dev)
         ms.append(s0.elapsed_time(e0))
-    return {"fused_cast_observe_ms": float(np.mean(ms)), "structure_band": list(band), "proximity": 2.0}
+    return {"cast_observe_ms": float(np.mean(ms)), "structure_band": list(band), "proximity": 2.0}
 
 
 def _band(scene_list) -> tuple[float, float]:

@@ -166,15 +166,17 @@ typedef struct tsdf_observe {
                                     proximity, structure band, forward structure band */
 } tsdf_observe;
 
-/* Device bytes of workspace tsdf_cast_fan_observe needs for n_actors. */
+/* Device bytes of workspace tsdf_cast_fan_observe needs for n_actors (the same as
+ * tsdf_fan_workspace_bytes). */
 TSDF_API uint64_t tsdf_observe_workspace_bytes(int64_t n_actors);
 
-/* tsdf_cast_fan plus the reference's post-processing fused into the ray writeback:
- * distances are clamped to [0, max_distance], depth = clamp(log1p(d) / log1p(max), 0, 1),
- * valid = isfinite(d); the observation tensor and the per-actor reductions
- * (_compute_observation_ratios_tensor, sdfdag_backend.py:366-405; min distance :459)
- * are written on `stream`.  Replaces _postprocess_cast_outputs_tensor
- * (sdfdag_backend.py:408-473) and the stack at :1518-1525. */
+/* tsdf_cast_fan plus the reference's post-processing, one pass over the cast's
+ * outputs on `stream` right after it (one block per actor): distances are clamped to
+ * [0, max_distance], depth = clamp(log1p(d) / log1p(max), 0, 1), valid = isfinite(d);
+ * the observation tensor and the per-actor reductions
+ * (_compute_observation_ratios_tensor, sdfdag_backend.py:366-405; min distance :459).
+ * Replaces _postprocess_cast_outputs_tensor (sdfdag_backend.py:408-473) and the stack
+ * at :1518-1525. */
 TSDF_API int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
                                    const float* fan_dirs, int64_t rays_per_actor, int use_pitch,
                                    float* out_dist, int32_t* out_sem, int32_t* out_steps, int max_steps,

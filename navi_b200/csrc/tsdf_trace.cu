@@ -74,17 +74,6 @@ struct TraceArgs {
     int32_t* out_s;
     int32_t* out_steps;
     unsigned int* counter;
-    // observation epilogue (fan launches with kObserve)
-    float* obs;                  // [actors][3][rays_per_actor]: depth, semantic, valid
-    unsigned int* obs_acc;       // [actors][6]: ~min key, NaN flag, saturated, proximity, band, forward band
-    uint32_t el_bins;
-    uint32_t az_bins;
-    uint32_t fwd_half;           // forward sector: azimuth rows [0, fwd_half) and [az - fwd_half, az)
-    float sat_thr;               // float32(max_distance - 1e-3)
-    float band_min, band_max;
-    float prox;
-    float inv_log_denom;         // float32(1 / log1p(max_distance)) (reciprocal in double)
-    int band_on, prox_on;
 };
 
 // Ray `r`: explicit origin/direction, or fan ray (actor, local direction) with the
@@ -165,77 +154,124 @@ __global__ void __launch_bounds__(1024) scene_sort_kernel(const float4* __restri
     }
 }
 
-// Epilogue of a finished ray (kernel.cu:298-308) plus, for kObserve, the reference's
-// post-processing of that ray (sdfdag_backend.py:436-446, :1518-1525) and its share of
-// the per-actor reductions (:366-405, :459).  The float steps are those of the torch ops
-// the reference runs: clamp = min(max(v, lo), hi) with NaN passed through, log1pf, and a
-// multiply by the scalar denominator's reciprocal (how torch divides by a host scalar).
-template <bool kObserve>
+// Epilogue of a finished ray (kernel.cu:298-308).
 __device__ __forceinline__ void finish_ray(const TraceArgs& a, uint32_t ray, float dist_out, int32_t sem_out,
                                            int32_t steps)
 {
     a.out_d[ray] = dist_out;
     a.out_s[ray] = sem_out;
     if (a.out_steps) a.out_steps[ray] = steps;
-    if constexpr (kObserve) {
-        const uint32_t R = a.rays_per_actor;
-        const uint32_t actor = ray / R;
-        const uint32_t k = ray - actor * R;
-        const bool valid = isfinite(dist_out);
-        const bool nan = isnan(dist_out);
-        float c = dist_out;
+}
+
+// Settings of the observation pass (tsdf_observe plus the derived constants).
+struct ObserveArgs {
+    uint32_t rays_per_actor;
+    uint32_t el_bins;
+    uint32_t az_bins;
+    uint32_t fwd_half;           // forward sector: azimuth rows [0, fwd_half) and [az - fwd_half, az)
+    float max_distance;
+    float sat_thr;               // float32(max_distance - 1e-3)
+    float band_min, band_max;
+    float prox;
+    float inv_log_denom;         // float32(1 / log1p(max_distance)) (reciprocal formed in double)
+    float f_all, f_fwd;          // torch's mean factors: float(A) / float(A * N)
+    int band_on, prox_on;
+};
+
+// The reference's post-processing of a fan cast, one block per actor over the actor's
+// finished rays: clamp to [0, max], depth = clamp(log1p(d) / log1p(max), 0, 1), valid =
+// isfinite (sdfdag_backend.py:436-446), the [A, 3, Az, El] stack (:1518-1525), and the
+// actor's minimum distance and ratios (:366-405, :459).  The float steps are those of the
+// torch ops the reference runs: clamp = min(max(v, lo), hi) with NaN passed through,
+// log1pf, and a multiply by the scalar denominator's reciprocal (how torch divides by a
+// host scalar); the ratios are counts times torch's mean factor.  A pass of its own
+// rather than an epilogue in the trace loop: there the finishing lanes of a warp iteration
+// are one or two, and the epilogue cost 8% of a config-2 launch.
+__global__ void __launch_bounds__(1024) observe_kernel(const float* __restrict__ dist, const int32_t* __restrict__ sem,
+                                                      float* __restrict__ obs, float* __restrict__ stats,
+                                                      const ObserveArgs o)
+{
+    const uint32_t actor = blockIdx.x;
+    const uint32_t R = o.rays_per_actor;
+    const float* dd = dist + static_cast<size_t>(actor) * R;
+    const int32_t* ss = sem + static_cast<size_t>(actor) * R;
+    float* ob = obs + static_cast<size_t>(actor) * 3u * R;
+    unsigned int nkey = 0, nan_any = 0, sat = 0, prox = 0, band = 0, fwd = 0;
+    for (uint32_t k = threadIdx.x; k < R; k += blockDim.x) {
+        const float d = dd[k];
+        const bool valid = isfinite(d);
+        const bool nan = isnan(d);
+        float c = d;
         if (!nan) {
             c = (c < 0.0f) ? 0.0f : c;
-            c = (a.max_distance < c) ? a.max_distance : c;
+            c = (o.max_distance < c) ? o.max_distance : c;
         }
-        float dep = __fmul_rn(log1pf(c), a.inv_log_denom);
+        float dep = __fmul_rn(log1pf(c), o.inv_log_denom);
         if (!isnan(dep)) {
             dep = (dep < 0.0f) ? 0.0f : dep;
             dep = (1.0f < dep) ? 1.0f : dep;
         }
-        float* o = a.obs + static_cast<size_t>(actor) * 3u * R + k;
-        o[0] = dep;
-        o[R] = static_cast<float>(sem_out);
-        o[2u * static_cast<size_t>(R)] = valid ? 1.0f : 0.0f;
-        unsigned int* acc = a.obs_acc + static_cast<size_t>(actor) * 6u;
+        ob[k] = dep;
+        ob[R + k] = static_cast<float>(ss[k]);
+        ob[2u * static_cast<size_t>(R) + k] = valid ? 1.0f : 0.0f;
         if (nan) {
-            atomicOr(acc + 1, 1u);
+            nan_any = 1u;
         } else {
             const unsigned int b = __float_as_uint(c);
             const unsigned int key = (b >> 31) ? ~b : (b | 0x80000000u);  // order-preserving
-            atomicMax(acc + 0, ~key);
+            nkey = max(nkey, ~key);
         }
-        if (c >= a.sat_thr) atomicAdd(acc + 2, 1u);
-        if (a.prox_on && valid && c <= a.prox) atomicAdd(acc + 3, 1u);
-        if (a.band_on && valid && c >= a.band_min && c <= a.band_max) {
-            atomicAdd(acc + 4, 1u);
-            const uint32_t az = k / a.el_bins;
-            const unsigned int fwd = (az < a.fwd_half ? 1u : 0u) + (az + a.fwd_half >= a.az_bins ? 1u : 0u);
-            if (fwd) atomicAdd(acc + 5, fwd);  // a row in both slices is counted twice, as torch.cat does
+        sat += (c >= o.sat_thr) ? 1u : 0u;
+        prox += (o.prox_on && valid && c <= o.prox) ? 1u : 0u;
+        if (o.band_on && valid && c >= o.band_min && c <= o.band_max) {
+            ++band;
+            const uint32_t az = k / o.el_bins;
+            // a row in both slices is counted twice, as torch.cat does
+            fwd += (az < o.fwd_half ? 1u : 0u) + (az + o.fwd_half >= o.az_bins ? 1u : 0u);
         }
     }
-}
-
-// Per-actor ratios as torch's mean computes them: sum * (float(A) / float(A * N)).
-__global__ void observe_finalize_kernel(const unsigned int* acc, float* stats, uint32_t actors, float f_all,
-                                        float f_fwd, int band_on, int prox_on)
-{
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= actors) return;
-    const unsigned int* c = acc + static_cast<size_t>(i) * 6u;
-    float mn;
-    if (c[1]) {
-        mn = __int_as_float(0x7fc00000);
-    } else {
-        const unsigned int key = ~c[0];
-        mn = __uint_as_float((key >> 31) ? (key & 0x7fffffffu) : ~key);
+    for (int off = 16; off > 0; off >>= 1) {
+        nkey = max(nkey, __shfl_xor_sync(kFull, nkey, off));
+        nan_any |= __shfl_xor_sync(kFull, nan_any, off);
+        sat += __shfl_xor_sync(kFull, sat, off);
+        prox += __shfl_xor_sync(kFull, prox, off);
+        band += __shfl_xor_sync(kFull, band, off);
+        fwd += __shfl_xor_sync(kFull, fwd, off);
     }
-    float* o = stats + static_cast<size_t>(i) * 5u;
-    o[0] = mn;
-    o[1] = fminf(fmaxf(__fmul_rn(static_cast<float>(c[2]), f_all), 0.0f), 1.0f);
-    o[2] = prox_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[3]), f_all), 0.0f), 1.0f) : 0.0f;
-    o[3] = band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[4]), f_all), 0.0f), 1.0f) : 0.0f;
-    o[4] = band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(c[5]), f_fwd), 0.0f), 1.0f) : 0.0f;
+    __shared__ unsigned int part[6][32];
+    const unsigned int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31u) == 0) {
+        part[0][w] = nkey;
+        part[1][w] = nan_any;
+        part[2][w] = sat;
+        part[3][w] = prox;
+        part[4][w] = band;
+        part[5][w] = fwd;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (unsigned int i = 1; i < (blockDim.x >> 5); ++i) {
+            nkey = max(nkey, part[0][i]);
+            nan_any |= part[1][i];
+            sat += part[2][i];
+            prox += part[3][i];
+            band += part[4][i];
+            fwd += part[5][i];
+        }
+        float mn;
+        if (nan_any) {
+            mn = __int_as_float(0x7fc00000);
+        } else {
+            const unsigned int key = ~nkey;
+            mn = __uint_as_float((key >> 31) ? (key & 0x7fffffffu) : ~key);
+        }
+        float* st = stats + static_cast<size_t>(actor) * 5u;
+        st[0] = mn;
+        st[1] = fminf(fmaxf(__fmul_rn(static_cast<float>(sat), o.f_all), 0.0f), 1.0f);
+        st[2] = o.prox_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(prox), o.f_all), 0.0f), 1.0f) : 0.0f;
+        st[3] = o.band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(band), o.f_all), 0.0f), 1.0f) : 0.0f;
+        st[4] = o.band_on ? fminf(fmaxf(__fmul_rn(static_cast<float>(fwd), o.f_fwd), 0.0f), 1.0f) : 0.0f;
+    }
 }
 
 __device__ __forceinline__ bool in_closed(const float3 p, const float3 mn, const float3 mx)
@@ -267,7 +303,7 @@ __device__ __forceinline__ float leaf_distance(uint32_t bits)
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xFFFFu)));
 }
 
-template <bool kFan, bool kMulti, bool kObserve = false>
+template <bool kFan, bool kMulti>
 __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a)
 {
     extern __shared__ __align__(16) uint32_t s_recs[];
@@ -345,7 +381,7 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                 if constexpr (kMulti) {
                     if (static_cast<uint32_t>(scene) >= a.n_scenes) {
                         // no such scene: the ray is not traced (NaN distance, semantic 0, 0 steps)
-                        finish_ray<kObserve>(a, ray, __int_as_float(0x7fc00000), 0, 0);
+                        finish_ray(a, ray, __int_as_float(0x7fc00000), 0, 0);
                         active = false;
                     } else {
                         const TsdfSceneDev* sc = a.table + scene;
@@ -455,13 +491,13 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
         if (step_done) {
             // ---- end of the march step (kernel.cu:297-304) ----
             if (sem != 0 && dist < eps) {
-                finish_ray<kObserve>(a, ray, t, sem, step + 1);
+                finish_ray(a, ray, t, sem, step + 1);
                 active = false;
             } else {
                 t = t + dist;
                 ++step;
                 if (t > a.max_distance || step >= a.max_steps) {
-                    finish_ray<kObserve>(a, ray, t, 0, step);
+                    finish_ray(a, ray, t, 0, step);
                     active = false;
                 }
             }
@@ -663,7 +699,7 @@ struct SceneAccess<true> {
     __device__ __forceinline__ float3 scale() const { return make_float3(__ldg(&s->scale[0]), __ldg(&s->scale[1]), __ldg(&s->scale[2])); }
 };
 
-template <bool kFan, bool kMulti, int kLevels, bool kObserve = false>
+template <bool kFan, bool kMulti, int kLevels>
 __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
@@ -743,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
             if constexpr (kMulti) {
                 if (static_cast<uint32_t>(scene) >= a.n_scenes) {
                     // no such scene: the ray is not traced (NaN distance, semantic 0, 0 steps)
-                    finish_ray<kObserve>(a, ray, __int_as_float(0x7fc00000), 0, 0);
+                    finish_ray(a, ray, __int_as_float(0x7fc00000), 0, 0);
                     active = false;
                 } else {
                     S.s = a.table + scene;
@@ -898,14 +934,14 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
             const float eps = S.eps();
             for (uint32_t run = 0;; ++run) {
                 if (sem != 0 && dist < eps) {
-                    finish_ray<kObserve>(a, ray, t, sem, step + 1);
+                    finish_ray(a, ray, t, sem, step + 1);
                     active = false;
                     break;
                 }
                 t = t + dist;
                 ++step;
                 if (t > a.max_distance || step >= a.max_steps) {
-                    finish_ray<kObserve>(a, ray, t, 0, step);
+                    finish_ray(a, ray, t, 0, step);
                     active = false;
                     break;
                 }
@@ -950,10 +986,10 @@ int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, f
 
 enum class Kind { kFloat, kGrid };
 
-constexpr size_t kObserveAccOffset = 256;  // per-actor accumulators follow the work counter
+constexpr size_t kPermOffset = 256;  // multi-scene actor order follows the work counter
 constexpr int64_t kSmemReservedPerBlock = 1024;  // shared memory the driver reserves per resident block
 
-template <bool kFan, bool kMulti, bool kObserve = false>
+template <bool kFan, bool kMulti>
 int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream)
 {
     cudaError_t e = cudaSetDevice(device);
@@ -964,11 +1000,11 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     void (*kern)(TraceArgs);
     size_t base;  // shared memory besides the staged records
     if (kind == Kind::kGrid) {
-        kern = trace_grid_kernel<kFan, kMulti, 3, kObserve>;
+        kern = trace_grid_kernel<kFan, kMulti, 3>;
         base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
         if (!kMulti) base += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
     } else {
-        kern = trace_float_kernel<kFan, kMulti, kObserve>;
+        kern = trace_float_kernel<kFan, kMulti>;
         base = 0;
     }
     // Stage no more top records than the register-limited occupancy leaves room for:
@@ -1003,9 +1039,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
     const int blocks = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(sms) * per_sm, need));
     a.counter = static_cast<unsigned int*>(workspace);
-    const size_t clear = kObserve ? kObserveAccOffset + static_cast<size_t>(a.n_rays / a.rays_per_actor) * 24u
-                                  : sizeof(unsigned int);
-    if (kObserve) a.obs_acc = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + kObserveAccOffset);
+    const size_t clear = sizeof(unsigned int);
     e = cudaMemsetAsync(workspace, 0, clear, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
     kern<<<blocks, kThreads, smem, stream>>>(a);
@@ -1153,7 +1187,7 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     }
     a.table = scenes->d_table;
     a.scene = scenes->host[0];
-    rc = sort_by_scene(a, scenes, n_actors, static_cast<char*>(workspace) + kObserveAccOffset,
+    rc = sort_by_scene(a, scenes, n_actors, static_cast<char*>(workspace) + kPermOffset,
                        static_cast<cudaStream_t>(stream));
     if (rc != TSDF_OK) return rc;
     return launch<true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace,
@@ -1162,12 +1196,12 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
 
 uint64_t tsdf_fan_workspace_bytes(int64_t n_actors)
 {
-    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 4u;
+    return n_actors <= 0 ? kPermOffset : kPermOffset + static_cast<uint64_t>(n_actors) * 4u;
 }
 
 uint64_t tsdf_observe_workspace_bytes(int64_t n_actors)
 {
-    return n_actors <= 0 ? kObserveAccOffset : kObserveAccOffset + static_cast<uint64_t>(n_actors) * 28u;
+    return tsdf_fan_workspace_bytes(n_actors);
 }
 
 int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_actors,
@@ -1207,23 +1241,26 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
     a.out_d = out_dist;
     a.out_s = out_sem;
     a.out_steps = out_steps;
-    a.obs = observe->observation;
-    a.az_bins = static_cast<uint32_t>(observe->azimuth_bins);
-    a.el_bins = static_cast<uint32_t>(observe->elevation_bins);
-    a.fwd_half = static_cast<uint32_t>(std::max(1, observe->azimuth_bins / 6));
+    ObserveArgs ob;
+    std::memset(&ob, 0, sizeof ob);
+    ob.rays_per_actor = a.rays_per_actor;
+    ob.az_bins = static_cast<uint32_t>(observe->azimuth_bins);
+    ob.el_bins = static_cast<uint32_t>(observe->elevation_bins);
+    ob.fwd_half = static_cast<uint32_t>(std::max(1, observe->azimuth_bins / 6));
+    ob.max_distance = max_distance;
     // the reference's scalars are Python floats: thresholds are formed in double, then
     // rounded to float32 by the tensor op; torch divides by the scalar log1p(max) by
     // multiplying with its reciprocal formed in double and rounded once to float32
-    a.sat_thr = static_cast<float>(static_cast<double>(max_distance) - 1e-3);
-    a.band_min = observe->structure_band_min;
-    a.band_max = observe->structure_band_max;
-    a.prox = observe->proximity_threshold;
-    a.band_on = observe->structure_band_max > observe->structure_band_min ? 1 : 0;
-    a.prox_on = observe->proximity_threshold > 0.0f ? 1 : 0;
-    a.inv_log_denom = static_cast<float>(1.0 / std::log1p(static_cast<double>(max_distance)));
+    ob.sat_thr = static_cast<float>(static_cast<double>(max_distance) - 1e-3);
+    ob.band_min = observe->structure_band_min;
+    ob.band_max = observe->structure_band_max;
+    ob.prox = observe->proximity_threshold;
+    ob.band_on = observe->structure_band_max > observe->structure_band_min ? 1 : 0;
+    ob.prox_on = observe->proximity_threshold > 0.0f ? 1 : 0;
+    ob.inv_log_denom = static_cast<float>(1.0 / std::log1p(static_cast<double>(max_distance)));
     const float fa = static_cast<float>(n_actors);
-    const float f_all = fa / static_cast<float>(n_rays);
-    const float f_fwd = fa / static_cast<float>(n_actors * 2 * static_cast<int64_t>(a.fwd_half) * observe->elevation_bins);
+    ob.f_all = fa / static_cast<float>(n_rays);
+    ob.f_fwd = fa / static_cast<float>(n_actors * 2 * static_cast<int64_t>(ob.fwd_half) * observe->elevation_bins);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (scenes->n == 1) {
         a.scene = scenes->host[0];
@@ -1231,22 +1268,22 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
                                                            static_cast<int64_t>(a.scene.n_recs)));
         const bool grid = scenes->grid && g_descent.load() == 0;
         if (!grid) a.scene.depth = -1;
-        rc = launch<true, false, true>(grid ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace, s);
+        rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace, s);
     } else {
         a.table = scenes->d_table;
         a.scene = scenes->host[0];
-        rc = sort_by_scene(a, scenes, n_actors,
-                           static_cast<char*>(workspace) + kObserveAccOffset + static_cast<size_t>(n_actors) * 24u, s);
+        rc = sort_by_scene(a, scenes, n_actors, static_cast<char*>(workspace) + kPermOffset, s);
         if (rc == TSDF_OK)
-            rc = launch<true, true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a,
-                                          scenes->device, workspace, s);
+            rc = launch<true, true>(scenes->grid && g_descent.load() == 0 ? Kind::kGrid : Kind::kFloat, a,
+                                    scenes->device, workspace, s);
     }
     if (rc != TSDF_OK) return rc;
-    const uint32_t actors = static_cast<uint32_t>(n_actors);
-    observe_finalize_kernel<<<(actors + 255u) / 256u, 256, 0, s>>>(a.obs_acc, observe->actor_stats, actors, f_all,
-                                                                   f_fwd, a.band_on, a.prox_on);
+    // one block per actor, up to 1024 threads: a few rays per thread even for small batches
+    const unsigned threads = static_cast<unsigned>(std::min<int64_t>(1024, std::max<int64_t>(32, (rays_per_actor + 31) / 32 * 32)));
+    observe_kernel<<<static_cast<unsigned>(n_actors), threads, 0, s>>>(out_dist, out_sem, observe->observation,
+                                                                       observe->actor_stats, ob);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "observe finalize launch");
+    if (e != cudaSuccess) return cuda_fail(e, "observation pass launch");
     return TSDF_OK;
 }
 

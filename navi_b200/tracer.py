@@ -431,7 +431,7 @@ def cast_fan_observe(
     use_pitch: bool = False,
     out_steps: torch.Tensor | None = None,
 ) -> None:
-    """cast_fan plus the reference's post-processing in the same kernel.
+    """cast_fan plus the reference's post-processing (one pass over the outputs, same stream).
 
     observation: [actors, 3, azimuth_bins, elevation_bins] f32 (depth, semantic, valid),
     as sdfdag_backend.py:1518-1525 stacks it; actor_stats: [actors, 5] f32 (min clamped
