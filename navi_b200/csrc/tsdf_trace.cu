@@ -61,6 +61,8 @@ struct TraceArgs {
     const float4* poses;         // fan rays: 2 float4 per actor (tsdf_pose)
     const float* fan;            // [rays_per_actor][3]
     uint32_t rays_per_actor;
+    uint32_t rpa_magic;          // r / rays_per_actor = (r * rpa_magic) >> rpa_shift for r < 2^31
+    uint32_t rpa_shift;
     int use_pitch;
     uint32_t n_rays;
     int max_steps;
@@ -76,13 +78,22 @@ struct TraceArgs {
     unsigned int* counter;
 };
 
+// Quotient by rays_per_actor without a division (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", 1994, theorem 4.2: for N-bit dividends, with
+// l = ceil(log2 d) and m = ceil(2^(N+l) / d), floor(n / d) = floor(m n / 2^(N+l)); here
+// N = 31, as ray indices are below 2^31, so m < 2^32).
+__device__ __forceinline__ uint32_t div_rpa(const TraceArgs& a, uint32_t r)
+{
+    return static_cast<uint32_t>((static_cast<uint64_t>(r) * a.rpa_magic) >> a.rpa_shift);
+}
+
 // Ray `r`: explicit origin/direction, or fan ray (actor, local direction) with the
 // reference's rotation (sdfdag_backend.py:1303-1310) and the optional pitch.
 template <bool kFan>
 __device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3& o, float3& d, int& scene)
 {
     if constexpr (kFan) {
-        const uint32_t actor = r / a.rays_per_actor;
+        const uint32_t actor = div_rpa(a, r);
         const uint32_t k = r - actor * a.rays_per_actor;
         const float4 p0 = __ldg(a.poses + 2 * static_cast<size_t>(actor));
         const float4 p1 = __ldg(a.poses + 2 * static_cast<size_t>(actor) + 1);
@@ -118,7 +129,7 @@ __device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w)
 {
     if constexpr (kFan && kMulti) {
         if (a.perm) {
-            const uint32_t slot = w / a.rays_per_actor;
+            const uint32_t slot = div_rpa(a, w);
             return __ldg(a.perm + slot) * a.rays_per_actor + (w - slot * a.rays_per_actor);
         }
     }
@@ -1087,6 +1098,17 @@ int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, voi
     return TSDF_OK;
 }
 
+// Multiplier and shift of div_rpa for rays_per_actor (>= 1).
+void set_rpa_divisor(TraceArgs& a)
+{
+    const uint32_t d = a.rays_per_actor ? a.rays_per_actor : 1u;
+    uint32_t l = 0;
+    while ((uint64_t(1) << l) < d) ++l;
+    const uint64_t num = uint64_t(1) << (31 + l);
+    a.rpa_magic = static_cast<uint32_t>((num + d - 1) / d);
+    a.rpa_shift = 31 + l;
+}
+
 uint32_t clamp_chunk()
 {
     const int64_t c = g_chunk.load();
@@ -1167,6 +1189,7 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     a.poses = reinterpret_cast<const float4*>(poses);
     a.fan = fan_dirs;
     a.rays_per_actor = static_cast<uint32_t>(rays_per_actor);
+    set_rpa_divisor(a);
     a.use_pitch = use_pitch ? 1 : 0;
     a.n_rays = static_cast<uint32_t>(n_rays);
     a.max_steps = max_steps;
@@ -1232,6 +1255,7 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
     a.poses = reinterpret_cast<const float4*>(poses);
     a.fan = fan_dirs;
     a.rays_per_actor = static_cast<uint32_t>(rays_per_actor);
+    set_rpa_divisor(a);
     a.use_pitch = use_pitch ? 1 : 0;
     a.n_rays = static_cast<uint32_t>(n_rays);
     a.max_steps = max_steps;

@@ -535,3 +535,30 @@ def test_tuning_options_do_not_change_results(opts):
         assert_bits_equal(gd, wd, f"dist under {opts}")
         assert_equal(gs, ws, f"sem under {opts}")
         assert_equal(gk, wk, f"steps under {opts}")
+
+
+@pytest.mark.parametrize("az,el,actors", [(1, 1, 5), (17, 5, 9), (255, 47, 3), (3, 1, 700)])
+def test_fan_sizes_and_actor_indexing(az, el, actors):
+    """Fans of any size: ray (actor, k) = index actor * (az * el) + k, checked against the
+    oracle on explicit rays (the kernel splits ray indices without a hardware division)."""
+    from navi_b200.fan import build_spherical_ray_directions
+
+    cs = workloads.compiled_scene(1)
+    pb = workloads.poses_for(1, [cs], actors=actors)
+    fan = torch.from_numpy(build_spherical_ray_directions(az, el)).to(dev())
+    poses = tracer.make_poses(torch.from_numpy(pb.position).to(dev()), torch.from_numpy(pb.yaw).to(dev()),
+                              torch.from_numpy(pb.pitch).to(dev()))
+    o, v = eager_world_rays(fan, poses, pitch=True)
+    sset = tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                           [cs.hit_epsilon])
+    n = actors * az * el
+    d = torch.empty(n, device=dev())
+    s = torch.empty(n, dtype=torch.int32, device=dev())
+    k = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, poses, fan, d, s, max_steps=128, max_distance=20.0, use_pitch=True, out_steps=k)
+    torch.cuda.synchronize()
+    ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, o.cpu().numpy(), v.cpu().numpy(), max_steps=128,
+                  max_distance=20.0, hit_epsilon=cs.hit_epsilon)
+    assert_bits_equal(d.cpu().numpy(), ref["dist"], "dist")
+    assert_equal(s.cpu().numpy(), ref["sem"], "sem")
+    assert_equal(k.cpu().numpy(), ref["steps"], "steps")
