@@ -15,8 +15,9 @@
   __constant__ (ref_shim_eps.cu says how).  The copied sources live in a
   scratch folder under oracle/_ref/ only while nvcc runs.
 
-The reference tree is read from $NAVI_REFERENCE_ROOT (default /root/reference);
-without it the prebuilt oracle/_ref files are used as they are.
+The reference tree is read from $NAVI_REFERENCE_ROOT (default: a directory named
+`reference` beside the repository); without it the prebuilt oracle/_ref files are used
+as they are.
 """
 
 from __future__ import annotations
@@ -36,7 +37,7 @@ EPS_NEW = "__constant__ float kHitEpsilon = 0.01f;"
 
 
 def _reference_root() -> Path:
-    return Path(os.environ.get("NAVI_REFERENCE_ROOT", "/root/reference"))
+    return Path(os.environ.get("NAVI_REFERENCE_ROOT", HERE.parent.parent / "reference"))
 
 
 def _ref_src() -> Path:
