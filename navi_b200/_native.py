@@ -7,11 +7,15 @@ loaded, every call that needs it raises RuntimeError.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
-TSDF_PATH = LIB_DIR / "libnavi_tsdf.so"
+# $NAVI_TSDF_DEBUG=1 selects the bounds-checked build (kernel indices checked, a device
+# error word reported by every call; slower)
+TSDF_PATH = LIB_DIR / ("libnavi_tsdf_debug.so" if os.environ.get("NAVI_TSDF_DEBUG", "0") not in ("", "0")
+                       else "libnavi_tsdf.so")
 GMDAG_PATH = LIB_DIR / "libnavi_gmdag.so"
 GMDAG_GPU_PATH = LIB_DIR / "libnavi_gmdag_gpu.so"
 

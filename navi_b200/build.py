@@ -4,6 +4,8 @@
 
 - libnavi_tsdf.so  : the sm_100a trace kernels and the C ABI of include/tsdf.h
                      (nvcc, -gencode arch=compute_100a,code=sm_100a, static cudart)
+- libnavi_tsdf_debug.so : the same with every kernel index bounds-checked
+                     (-DTSDF_BOUNDS_CHECK; selected by $NAVI_TSDF_DEBUG=1)
 - libnavi_gmdag.so : the host scene compiler (g++, OpenMP, -ffp-contract=off so
                      that its float arithmetic matches the reference compiler's)
 - libnavi_gmdag_gpu.so : the device scene compiler (nvcc sm_100a, -fmad=false,
@@ -64,8 +66,11 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build command failed ({proc.returncode}): {' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
 
 
-def build_tsdf(force: bool = False) -> Path:
-    out = LIB / "libnavi_tsdf.so"
+def build_tsdf(force: bool = False, bounds_check: bool = False) -> Path:
+    """libnavi_tsdf.so, or with bounds_check libnavi_tsdf_debug.so: the same library with
+    every pool, leaf-table, stack and actor-order index checked in the kernels (a device
+    error word, reported by the call) — the stand-in for compute-sanitizer runs."""
+    out = LIB / ("libnavi_tsdf_debug.so" if bounds_check else "libnavi_tsdf.so")
     srcs = [CSRC / "tsdf_trace.cu", CSRC / "tsdf_pool.cpp", CSRC / "gmdag_io.cpp"]
     deps = srcs + [CSRC / "tsdf_internal.h", CSRC / "gmdag_io.h", INCLUDE / "tsdf.h", INCLUDE / "gmdag.h"]
     if force or _stale(out, deps):
@@ -74,6 +79,7 @@ def build_tsdf(force: bool = False) -> Path:
         _run([
             _nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
             "-Xcompiler", "-fvisibility=hidden", "-Xlinker", "--exclude-libs,ALL", "-diag-suppress", "186",
+            *(["-DTSDF_BOUNDS_CHECK"] if bounds_check else []),
             f"-I{INCLUDE}", *map(str, srcs), "-o", str(tmp),
         ])
         tmp.replace(out)
@@ -114,7 +120,7 @@ def build_gmdag_gpu(force: bool = False) -> Path:
 
 
 def build_all(force: bool = False) -> list[Path]:
-    return [build_tsdf(force), build_gmdag(force), build_gmdag_gpu(force)]
+    return [build_tsdf(force), build_tsdf(force, bounds_check=True), build_gmdag(force), build_gmdag_gpu(force)]
 
 
 if __name__ == "__main__":

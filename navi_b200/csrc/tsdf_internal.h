@@ -90,7 +90,7 @@ struct TsdfSceneDev {
     float eps;
     int32_t depth;                   // grid depth D (cells per axis 2^D); -1: float descent
     float scale[3];                  // 2^D / (bmax - bmin) per axis, float division
-    float pad_;
+    uint32_t n_ext;                  // out-of-line leaves (bounds-checked builds)
 };
 static_assert(sizeof(TsdfSceneDev) == 80, "scene record layout");
 

@@ -557,6 +557,7 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
         d.ext = p->d_ext;
         d.root = p->root;
         d.n_recs = static_cast<uint32_t>(p->records);
+        d.n_ext = static_cast<uint32_t>(p->ext);
         for (int a = 0; a < 3; ++a) {
             d.bmin[a] = bbox_min[3 * i + a];
             d.bmax[a] = bbox_max[3 * i + a];

@@ -22,6 +22,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -76,7 +77,32 @@ struct TraceArgs {
     int32_t* out_s;
     int32_t* out_steps;
     unsigned int* counter;
+    unsigned int* err;           // bounds-checked builds: error bits (word after the counter)
 };
+
+// Bounds-checked builds (TSDF_BOUNDS_CHECK, libnavi_tsdf_debug.so): every node-pool,
+// leaf-table, stack and actor-order index is checked before it is used; a failed check
+// sets a bit of the error word and the access is replaced by a harmless one (an empty
+// octant, leaf 0, no stack write), so the launch finishes and the host reports the
+// bits.  The pools are validated when they are built, so a set bit means a bug in
+// this library.  In the regular build the checks compile to nothing.
+#ifdef TSDF_BOUNDS_CHECK
+constexpr bool kBoundsCheck = true;
+#else
+constexpr bool kBoundsCheck = false;
+#endif
+constexpr unsigned int kErrRecord = 1u, kErrLeafTable = 2u, kErrStack = 4u, kErrActor = 8u;
+
+__device__ __forceinline__ bool checked(unsigned int* err, bool ok, unsigned int bit)
+{
+    if constexpr (kBoundsCheck) {
+        if (!ok) {
+            atomicOr(err, bit);
+            return false;
+        }
+    }
+    return true;
+}
 
 // Quotient by rays_per_actor without a division (Granlund and Montgomery, "Division by
 // invariant integers using multiplication", 1994, theorem 4.2: for N-bit dividends, with
@@ -130,7 +156,9 @@ __device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w)
     if constexpr (kFan && kMulti) {
         if (a.perm) {
             const uint32_t slot = div_rpa(a, w);
-            return __ldg(a.perm + slot) * a.rays_per_actor + (w - slot * a.rays_per_actor);
+            uint32_t actor = __ldg(a.perm + slot);
+            if (!checked(a.err, actor < a.n_rays / a.rays_per_actor, kErrActor)) actor = 0;
+            return actor * a.rays_per_actor + (w - slot * a.rays_per_actor);
         }
     }
     return w;
@@ -350,6 +378,7 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
     const uint32_t* recs = a.scene.recs;
     const uint64_t* ext = a.scene.ext;
     uint32_t root = a.scene.root;
+    uint32_t n_recs = a.scene.n_recs, n_ext = a.scene.n_ext;
     float3 bmn = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
     float3 bmx = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
     float eps = a.scene.eps;
@@ -397,6 +426,8 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                     } else {
                         const TsdfSceneDev* sc = a.table + scene;
                         recs = sc->recs;
+                        n_recs = sc->n_recs;
+                        n_ext = sc->n_ext;
                         ext = sc->ext;
                         root = sc->root;
                         bmn = make_float3(sc->bmin[0], sc->bmin[1], sc->bmin[2]);
@@ -450,8 +481,9 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                 leaf = node & ~tsdf::kSlotLeafBit;
                 is_leaf = true;
             } else if (node & tsdf::kSlotExtBit) {
-                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(ext) +
-                                                   (node & tsdf::kSlotIndexMask)));
+                if (checked(a.err, (node & tsdf::kSlotIndexMask) < n_ext, kErrLeafTable))
+                    leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(ext) +
+                                                       (node & tsdf::kSlotIndexMask)));
                 is_leaf = true;
             } else {
                 if (depth == kPrefixDepth && !(flags & kUsePre)) {
@@ -469,7 +501,8 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                 if (uy) cmn.y = my_; else cmx.y = my_;
                 if (uz) cmn.z = mz_; else cmx.z = mz_;
                 const size_t si = static_cast<size_t>(node) * 8u + oct;
-                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(recs + si);
+                uint32_t slot = tsdf::kSlotVoid;
+                if (checked(a.err, node < n_recs, kErrRecord)) slot = (node < n_smem) ? s_recs[si] : __ldg(recs + si);
                 if (slot == tsdf::kSlotVoid) {
                     vmn = cmn;
                     vmx = cmx;
@@ -676,6 +709,8 @@ struct SceneAccess<false> {
     __device__ __forceinline__ const uint32_t* recs() const { return s->recs; }
     __device__ __forceinline__ const uint64_t* ext() const { return s->ext; }
     __device__ __forceinline__ uint32_t root() const { return s->root; }
+    __device__ __forceinline__ uint32_t n_recs() const { return s->n_recs; }
+    __device__ __forceinline__ uint32_t n_ext() const { return s->n_ext; }
     __device__ __forceinline__ int depth() const { return s->depth; }
     __device__ __forceinline__ float eps() const { return s->eps; }
     __device__ __forceinline__ GridView grid() const { return g; }
@@ -696,6 +731,8 @@ struct SceneAccess<true> {
         return reinterpret_cast<const uint64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&s->ext)));
     }
     __device__ __forceinline__ uint32_t root() const { return __ldg(&s->root); }
+    __device__ __forceinline__ uint32_t n_recs() const { return __ldg(&s->n_recs); }
+    __device__ __forceinline__ uint32_t n_ext() const { return __ldg(&s->n_ext); }
     __device__ __forceinline__ int depth() const { return __ldg(&s->depth); }
     __device__ __forceinline__ float eps() const { return __ldg(&s->eps); }
     __device__ __forceinline__ GridView grid() const
@@ -845,7 +882,7 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
                 int level;
                 if (reuse >= start && reuse >= sv) {
                     level = reuse;
-                    node = my_stack[level * kThreads];
+                    node = checked(a.err, level < kStackLevels, kErrStack) ? my_stack[level * kThreads] : S.root();
                     if (!use_pre && level > kPrefixDepth) {
                         pre_rec = my_stack[kPrefixDepth * kThreads];
                         pcx = pack_cell(jx, D - kPrefixDepth);
@@ -875,11 +912,12 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
                 leaf = node & ~tsdf::kSlotLeafBit;
                 is_leaf = true;
             } else if (node & tsdf::kSlotExtBit) {
-                leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
-                                                   (node & tsdf::kSlotIndexMask)));
+                if (checked(a.err, (node & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable))
+                    leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
+                                                       (node & tsdf::kSlotIndexMask)));
                 is_leaf = true;
             } else {
-                my_stack[level * kThreads] = node;
+                if (checked(a.err, level < kStackLevels, kErrStack)) my_stack[level * kThreads] = node;
                 if (level == kPrefixDepth && !(flags & kUsePre)) {
                     pre_rec = node;
                     pcx = pack_cell(jx, D - kPrefixDepth);
@@ -890,7 +928,9 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
                 const int sh = D - 1 - level;
                 const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
                 const size_t si = static_cast<size_t>(node) * 8u + oct;
-                const uint32_t slot = (node < n_smem) ? s_recs[si] : __ldg(S.recs() + si);
+                uint32_t slot = tsdf::kSlotVoid;
+                if (checked(a.err, node < S.n_recs(), kErrRecord))
+                    slot = (node < n_smem) ? s_recs[si] : __ldg(S.recs() + si);
                 leaf_level = level + 1;
                 if (slot == tsdf::kSlotVoid) {
                     vcx = pack_cell(jx, D - leaf_level);
@@ -1050,12 +1090,24 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
     const int blocks = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(sms) * per_sm, need));
     a.counter = static_cast<unsigned int*>(workspace);
-    const size_t clear = sizeof(unsigned int);
+    a.err = a.counter + 1;
+    const size_t clear = 2 * sizeof(unsigned int);
     e = cudaMemsetAsync(workspace, 0, clear, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
     kern<<<blocks, kThreads, smem, stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "trace kernel launch");
+    if constexpr (kBoundsCheck) {
+        unsigned int bits = 0;
+        e = cudaMemcpyAsync(&bits, a.err, sizeof bits, cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e, "reading the bounds-check word");
+        if (bits) {
+            char msg[96];
+            std::snprintf(msg, sizeof msg, "bounds check failed in the trace kernel (bits 0x%x)", bits);
+            return fail(TSDF_ERR_LAYOUT, msg);
+        }
+    }
     return TSDF_OK;
 }
 
@@ -1143,6 +1195,7 @@ int tsdf_cast(const tsdf_pool* pool, const float* origins, const float* dirs, in
     a.scene.ext = pool->d_ext;
     a.scene.root = pool->root;
     a.scene.n_recs = static_cast<uint32_t>(pool->records);
+    a.scene.n_ext = static_cast<uint32_t>(pool->ext);
     for (int i = 0; i < 3; ++i) {
         a.scene.bmin[i] = bbox_min[i];
         a.scene.bmax[i] = bbox_max[i];
@@ -1438,6 +1491,7 @@ extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, co
     a.scene.ext = pool->d_ext;
     a.scene.root = pool->root;
     a.scene.n_recs = static_cast<uint32_t>(pool->records);
+    a.scene.n_ext = static_cast<uint32_t>(pool->ext);
     for (int i = 0; i < 3; ++i) {
         a.scene.bmin[i] = bbox_min[i];
         a.scene.bmax[i] = bbox_max[i];

@@ -13,9 +13,11 @@ non-CUDA tensor raises RuntimeError.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import hashlib
 import math
+import os
 import threading
 import weakref
 from dataclasses import dataclass
@@ -43,6 +45,22 @@ __all__ = [
 ]
 
 DEFAULT_HIT_EPSILON = 0.01
+
+
+_NVTX = os.environ.get("NAVI_NVTX", "0") not in ("", "0")
+
+
+@contextlib.contextmanager
+def _nvtx(name: str):
+    """An NVTX range around a native call when $NAVI_NVTX is set (for nsight timelines)."""
+    if not _NVTX:
+        yield
+        return
+    torch.cuda.nvtx.range_push(name)
+    try:
+        yield
+    finally:
+        torch.cuda.nvtx.range_pop()
 
 
 def _stream_handle(device: torch.device) -> int:
@@ -231,14 +249,15 @@ def cast_rays_ex(
     _same_device(pool.device, origins, dirs, out_distances, out_semantics, out_steps)
     ws = workspace(pool.device)
     lib = _native.tsdf_lib()
-    rc = lib.tsdf_cast(
-        pool.handle,
-        ctypes.c_void_p(origins.data_ptr()), ctypes.c_void_p(dirs.data_ptr()), n,
-        ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
-        ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None),
-        int(max_steps), float(max_distance), _bbox3(bbox_min, "bbox_min"), _bbox3(bbox_max, "bbox_max"),
-        float(hit_epsilon), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(pool.device)),
-    )
+    with _nvtx("tsdf_cast"):
+        rc = lib.tsdf_cast(
+            pool.handle,
+            ctypes.c_void_p(origins.data_ptr()), ctypes.c_void_p(dirs.data_ptr()), n,
+            ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
+            ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None),
+            int(max_steps), float(max_distance), _bbox3(bbox_min, "bbox_min"), _bbox3(bbox_max, "bbox_max"),
+            float(hit_epsilon), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(pool.device)),
+        )
     _native.check(rc, "tsdf_cast")
 
 
@@ -403,12 +422,13 @@ def cast_fan(
     _same_device(scenes.device, poses, fan_dirs, out_distances, out_semantics, out_steps)
     lib = _native.tsdf_lib()
     ws = torch.empty(int(lib.tsdf_fan_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
-    rc = lib.tsdf_cast_fan(
-        scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
-        1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
-        ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None), int(max_steps),
-        float(max_distance), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
-    )
+    with _nvtx("tsdf_cast_fan"):
+        rc = lib.tsdf_cast_fan(
+            scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
+            1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
+            ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None), int(max_steps),
+            float(max_distance), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
+        )
     _native.check(rc, "tsdf_cast_fan")
 
 
@@ -455,12 +475,13 @@ def cast_fan_observe(
     ws = torch.empty(int(lib.tsdf_observe_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
     ob = _native.Observe(int(azimuth_bins), int(elevation_bins), float(structure_band_min), float(structure_band_max),
                          float(proximity_threshold), observation.data_ptr(), actor_stats.data_ptr())
-    rc = lib.tsdf_cast_fan_observe(
-        scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
-        1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
-        ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None), int(max_steps), float(max_distance),
-        ctypes.byref(ob), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
-    )
+    with _nvtx("tsdf_cast_fan_observe"):
+        rc = lib.tsdf_cast_fan_observe(
+            scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
+            1 if use_pitch else 0, ctypes.c_void_p(out_distances.data_ptr()), ctypes.c_void_p(out_semantics.data_ptr()),
+            ctypes.c_void_p(out_steps.data_ptr() if out_steps is not None else None), int(max_steps), float(max_distance),
+            ctypes.byref(ob), ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(_stream_handle(scenes.device)),
+        )
     _native.check(rc, "tsdf_cast_fan_observe")
 
 
