@@ -484,7 +484,8 @@ def run_navi(args) -> None:
                 "pool_bytes": int(sum(p.stats["device_bytes"] for p in pools)),
                 "descent": args.descent,
             },
-            "gpu_launches": args.steps,
+            # per step: the trace kernel, plus the scene-order sort for scene tables of more than one scene
+            "gpu_launches": args.steps * (2 if len(scene_list) > 1 else 1),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "e2e_fan": e2e_fan,
