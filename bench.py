@@ -50,6 +50,8 @@ def _args() -> argparse.Namespace:
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["navi", "reference"], default="navi")
     ap.add_argument("--pose-sets", type=int, default=4, help="distinct pose sets cycled over the steps")
+    ap.add_argument("--actors", type=int, default=0,
+                    help="actors per rank instead of the configuration's (0 = the configuration's; for small profiles)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-actors", type=int, default=0, help="actors in the CPU-baseline sample (0 = auto)")
@@ -141,14 +143,14 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- workload
 
 
-def _workload(config: int, rank: int, world: int, pose_sets: int):
+def _workload(config: int, rank: int, world: int, pose_sets: int, actors_override: int = 0):
     """Scenes (compiled, cached) and this rank's pose sets."""
     from navi_b200 import scenes, workloads
 
     cfg = scenes.CONFIGS[config]
     scene_list = [workloads.compiled_scene(config, s) for s in range(cfg.n_scenes)]
     strong = config == 5
-    actors = cfg.actors // world if strong else cfg.actors
+    actors = actors_override or (cfg.actors // world if strong else cfg.actors)
     sets = [workloads.poses_for(config, scene_list, actors=actors, seed_offset=1 + 7919 * rank + 104729 * k)
             for k in range(pose_sets)]
     return cfg, scene_list, sets, strong
@@ -198,7 +200,7 @@ def run_reference(args) -> None:
     from oracle import build as OB
 
     OB.build_oracle()
-    cfg, scene_list, sets, _strong = _workload(args.config, 0, 1, 1)
+    cfg, scene_list, sets, _strong = _workload(args.config, 0, 1, 1, args.actors)
     from navi_b200.fan import build_spherical_ray_directions
 
     fan = build_spherical_ray_directions(cfg.azimuth_bins, cfg.elevation_bins)
@@ -357,7 +359,7 @@ def run_navi(args) -> None:
     # rank 0 compiles (and caches) the scenes first; the others then read the cache
     if dist is not None and rank != 0:
         dist.barrier()
-    cfg, scene_list, sets, strong = _workload(args.config, rank, world, args.pose_sets)
+    cfg, scene_list, sets, strong = _workload(args.config, rank, world, args.pose_sets, args.actors)
     if dist is not None and rank == 0:
         dist.barrier()
 
