@@ -562,3 +562,92 @@ def test_fan_sizes_and_actor_indexing(az, el, actors):
     assert_bits_equal(d.cpu().numpy(), ref["dist"], "dist")
     assert_equal(s.cpu().numpy(), ref["sem"], "sem")
     assert_equal(k.cpu().numpy(), ref["steps"], "steps")
+
+
+def _multiscene_setup(config, actors=None):
+    cfg = scenes.CONFIGS[config]
+    scene_list = [workloads.compiled_scene(config, s) for s in range(cfg.n_scenes)]
+    pb = workloads.poses_for(config, scene_list, actors=actors)
+    fan = torch.from_numpy(workloads.fan_for(config)).to(dev())
+    pools = [tracer.NodePool.from_words(cs.words, dev()) for cs in scene_list]
+    sset = tracer.SceneSet(pools, [c.bbox_min for c in scene_list], [c.bbox_max for c in scene_list],
+                           [c.hit_epsilon for c in scene_list])
+    return cfg, scene_list, pb, fan, pools, sset
+
+
+def _poses(pb, sel, scene_ids):
+    return tracer.make_poses(torch.from_numpy(pb.position[sel]).to(dev()), torch.from_numpy(pb.yaw[sel]).to(dev()),
+                             torch.from_numpy(pb.pitch[sel]).to(dev()), torch.from_numpy(scene_ids).to(dev()))
+
+
+def _sampled_oracle_check(cfg, scene_list, pb, fan, d, s, k, n_sample, seed):
+    rng = np.random.default_rng(seed)
+    r = fan.shape[0]
+    rays = np.sort(rng.choice(pb.position.shape[0] * r, size=n_sample, replace=False))
+    actor, ki = rays // r, rays % r
+    fan_np = fan.cpu().numpy()
+    # the cos/sin the kernel uses: torch.cos / torch.sin on the device, as in the poses
+    pose = _poses(pb, np.arange(pb.position.shape[0]), pb.scene).cpu().numpy()
+    dirs = O.rotate_fan(fan_np, pose[:, 3], pose[:, 4])
+    for sc in np.unique(pb.scene[actor]):
+        m = pb.scene[actor] == sc
+        cs = scene_list[sc]
+        o = pb.position[actor[m]]
+        v = dirs[actor[m], ki[m]]
+        ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, o, v, max_steps=cfg.max_steps,
+                      max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+        assert_bits_equal(d[rays[m]], ref["dist"], f"dist scene {sc}")
+        assert_equal(s[rays[m]], ref["sem"], f"sem scene {sc}")
+        assert_equal(k[rays[m]], ref["steps"], f"steps scene {sc}")
+
+
+def test_config3_full_step_multiscene_equals_per_scene_launches_and_oracle():
+    """Config 3 at full size (8 scenes, 4096 actors x 3072 rays = 12.6 M rays): one
+    multi-scene launch equals the eight single-scene launches of the same actors bit for
+    bit; 200,000 sampled rays equal the oracle."""
+    cfg, scene_list, pb, fan, pools, sset = _multiscene_setup(3)
+    a, r = pb.position.shape[0], fan.shape[0]
+    n = a * r
+    d = torch.empty(n, device=dev())
+    s = torch.empty(n, dtype=torch.int32, device=dev())
+    k = torch.empty(n, dtype=torch.int32, device=dev())
+    tracer.cast_fan(sset, _poses(pb, np.arange(a), pb.scene), fan, d, s, max_steps=cfg.max_steps,
+                    max_distance=cfg.max_distance, out_steps=k)
+    torch.cuda.synchronize()
+    d, s, k = (x.cpu().numpy().reshape(a, r) for x in (d, s, k))
+    for sc, cs in enumerate(scene_list):
+        sel = np.nonzero(pb.scene == sc)[0]
+        one = tracer.SceneSet([pools[sc]], [cs.bbox_min], [cs.bbox_max], [cs.hit_epsilon])
+        m = sel.shape[0] * r
+        ds = torch.empty(m, device=dev())
+        ss = torch.empty(m, dtype=torch.int32, device=dev())
+        ks = torch.empty(m, dtype=torch.int32, device=dev())
+        tracer.cast_fan(one, _poses(pb, sel, np.zeros(sel.shape[0], np.int32)), fan, ds, ss, max_steps=cfg.max_steps,
+                        max_distance=cfg.max_distance, out_steps=ks)
+        torch.cuda.synchronize()
+        assert_bits_equal(d[sel].reshape(-1), ds.cpu().numpy(), f"scene {sc} dist")
+        assert_equal(s[sel].reshape(-1), ss.cpu().numpy(), f"scene {sc} sem")
+        assert_equal(k[sel].reshape(-1), ks.cpu().numpy(), f"scene {sc} steps")
+    _sampled_oracle_check(cfg, scene_list, pb, fan, d.reshape(-1), s.reshape(-1), k.reshape(-1), 200_000, 3)
+
+
+def test_config5_step_sampled_oracle_and_determinism():
+    """Config 5's scenes and fan (16 scenes, 256 x 48 rays) for 4096 actors (50 M rays, the
+    per-rank share at 8 GPUs): 200,000 sampled rays equal the oracle; a second launch gives
+    the same bits."""
+    cfg, scene_list, pb, fan, pools, sset = _multiscene_setup(5, actors=4096)
+    a, r = pb.position.shape[0], fan.shape[0]
+    n = a * r
+    poses = _poses(pb, np.arange(a), pb.scene)
+    outs = []
+    for _ in range(2):
+        d = torch.empty(n, device=dev())
+        s = torch.empty(n, dtype=torch.int32, device=dev())
+        k = torch.empty(n, dtype=torch.int32, device=dev())
+        tracer.cast_fan(sset, poses, fan, d, s, max_steps=cfg.max_steps, max_distance=cfg.max_distance, out_steps=k)
+        torch.cuda.synchronize()
+        outs.append((d.cpu().numpy(), s.cpu().numpy(), k.cpu().numpy()))
+        del d, s, k
+    assert_bits_equal(outs[0][0], outs[1][0], "repeat dist")
+    assert_equal(outs[0][2], outs[1][2], "repeat steps")
+    _sampled_oracle_check(cfg, scene_list, pb, fan, *outs[0], 200_000, 5)
