@@ -151,8 +151,11 @@ def _workload(config: int, rank: int, world: int, pose_sets: int, actors_overrid
     scene_list = [workloads.compiled_scene(config, s) for s in range(cfg.n_scenes)]
     strong = config == 5
     actors = actors_override or (cfg.actors // world if strong else cfg.actors)
-    sets = [workloads.poses_for(config, scene_list, actors=actors, seed_offset=1 + 7919 * rank + 104729 * k)
-            for k in range(pose_sets)]
+    if config == 5:  # poses re-drawn each step by a random walk (0.1 m, yaw jitter N(0, 5 deg))
+        sets = workloads.walk_pose_sets(config, scene_list, pose_sets, actors=actors, seed_offset=1 + 7919 * rank)
+    else:
+        sets = [workloads.poses_for(config, scene_list, actors=actors, seed_offset=1 + 7919 * rank + 104729 * k)
+                for k in range(pose_sets)]
     return cfg, scene_list, sets, strong
 
 
@@ -481,6 +484,8 @@ def run_navi(args) -> None:
                 "max_distance": cfg.max_distance,
                 "hit_epsilon": "1e-3 x voxel",
                 "pitch_deg": cfg.pitch_deg,
+                "poses": (f"random walk: {args.pose_sets} successive steps cycled" if args.config == 5
+                          else f"uniform in free space: {args.pose_sets} independent sets cycled"),
                 "parallelism": f"dp{world} (scene replica per GPU, no hot-path collective)",
                 "l2": "flushed between steps (2 x L2 bytes written), outside the timed events",
                 "pool_bytes": int(sum(p.stats["device_bytes"] for p in pools)),

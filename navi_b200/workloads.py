@@ -125,3 +125,17 @@ def poses_for(config: int, scene_list: list[CompiledScene], actors: int | None =
 def fan_for(config: int) -> np.ndarray:
     cfg = scenes.CONFIGS[config]
     return build_spherical_ray_directions(cfg.azimuth_bins, cfg.elevation_bins)
+
+
+def walk_pose_sets(config: int, scene_list: list[CompiledScene], n_sets: int, actors: int | None = None,
+                   seed_offset: int = 0) -> list[PoseBatch]:
+    """Successive poses of a random walk (configuration 5: 0.1 m steps, yaw jitter N(0, 5 deg),
+    moves that leave free space rejected): a uniform draw, then n_sets - 1 walk steps."""
+    first = poses_for(config, scene_list, actors=actors, seed_offset=seed_offset)
+    sets = [first]
+    meshes = [cs.mesh for cs in scene_list]
+    cur = {"position": first.position, "yaw": first.yaw, "pitch": first.pitch}
+    for k in range(1, n_sets):
+        cur = scenes.random_walk_poses(meshes, first.scene, cur, seed=1000 * config + 777 + 31 * k + seed_offset)
+        sets.append(PoseBatch(cur["position"], cur["yaw"], cur["pitch"], first.scene))
+    return sets
