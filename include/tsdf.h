@@ -114,9 +114,10 @@ TSDF_API int tsdf_pool_load(const char* path, int device, tsdf_pool** out_pool);
 TSDF_API int tsdf_pool_destroy(tsdf_pool* pool);
 TSDF_API int tsdf_pool_stats_get(const tsdf_pool* pool, tsdf_pool_stats* out);
 
-/* Device bytes of scratch that tsdf_cast / tsdf_cast_fan need in `workspace`
- * (a work counter); the caller allocates it, on the device of the pool. */
-TSDF_API uint64_t tsdf_workspace_bytes(void);
+/* Device bytes of scratch that tsdf_cast needs in `workspace` for n_rays rays; the
+ * caller allocates it (16-byte aligned), on the device of the pool.  It holds the work
+ * counter and the claim order: 256 + 512 + 5 * n_rays bytes, rounded up to 16. */
+TSDF_API uint64_t tsdf_workspace_bytes(int64_t n_rays);
 
 /* Explicit-ray cast: the semantics of sphere_trace_kernel (kernel.cu:203-309)
  * for rays [n_rays][3] origins / dirs (f32, device), writing distance (f32),
@@ -135,16 +136,19 @@ TSDF_API int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const floa
                        const float* bbox_max, const float* hit_epsilon, tsdf_scenes** out);
 TSDF_API int tsdf_scenes_destroy(tsdf_scenes* scenes);
 
-/* Device bytes of workspace tsdf_cast_fan needs for n_actors: the work counter
- * and, for scene tables of more than one scene, the actor order by scene. */
-TSDF_API uint64_t tsdf_fan_workspace_bytes(int64_t n_actors);
+/* Device bytes of workspace tsdf_cast_fan needs for n_actors x rays_per_actor rays
+ * on `scenes`: the work counter and, for a table of one scene, the claim order (as
+ * tsdf_workspace_bytes), for more than one scene the actor order by scene (4 bytes
+ * per actor).  scenes = NULL gives the larger of the two. */
+TSDF_API uint64_t tsdf_fan_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors,
+                                           int64_t rays_per_actor);
 
 /* Fused fan cast: ray (a, r) starts at pose a's origin with the local fan
  * direction fan_dirs[r] (device, [rays_per_actor][3] f32), pitched about the
  * local x axis when use_pitch != 0, then yaw-rotated as
  * sdfdag_backend.py:1303-1310 does, and is traced in scene poses[a].scene.
  * Outputs are [n_actors * rays_per_actor], actor-major.  workspace:
- * tsdf_fan_workspace_bytes(n_actors) bytes on the scenes' device.  Multi-scene
+ * tsdf_fan_workspace_bytes(scenes, n_actors, rays_per_actor) bytes on the scenes' device.  Multi-scene
  * tables trace the actors grouped by scene (the outputs do not depend on the
  * order); an actor whose scene index is outside the table is not traced: its
  * rays get a NaN distance, semantic 0 and 0 steps. */
@@ -166,9 +170,10 @@ typedef struct tsdf_observe {
                                     proximity, structure band, forward structure band */
 } tsdf_observe;
 
-/* Device bytes of workspace tsdf_cast_fan_observe needs for n_actors (the same as
+/* Device bytes of workspace tsdf_cast_fan_observe needs (the same as
  * tsdf_fan_workspace_bytes). */
-TSDF_API uint64_t tsdf_observe_workspace_bytes(int64_t n_actors);
+TSDF_API uint64_t tsdf_observe_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors,
+                                               int64_t rays_per_actor);
 
 /* tsdf_cast_fan plus the reference's post-processing, one pass over the cast's
  * outputs on `stream` right after it (one block per actor): distances are clamped to
@@ -191,7 +196,8 @@ TSDF_API int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* p
  * loads it; its address is looked up by the first call on each device, which
  * must come before any stream capture.  All calls share that array: calls whose
  * kernels may overlap on the GPU race and must be ordered on one stream.
- * Allocates nothing: no cudaMalloc, no cudaFree. */
+ * Allocates nothing: no cudaMalloc, no cudaFree.  With no room for a claim order,
+ * rays are claimed in index order. */
 TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, const float* dirs,
                                int64_t n_rays, float* out_dist, int32_t* out_sem, int32_t* out_steps,
                                int max_steps, float max_distance, const float bbox_min[3],
@@ -203,7 +209,9 @@ TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, cons
  * at once, default 8), "leaf_run" (leaf-cache steps a single-scene lane takes in
  * place after a step, default 1), "blocks_per_sm" (0 = occupancy maximum),
  * "descent" (0 = integer grid descent wherever the DAG allows it, 1 = float
- * descent only).  No knob changes results.  Returns the old value through
+ * descent only), "order" (single-scene claim order: 1 = rays that can travel
+ * farthest inside the scene box are claimed first, the default; 0 = ray index
+ * order).  No knob changes results.  Returns the old value through
  * *old_value when not NULL. */
 TSDF_API int tsdf_set_option(const char* key, int64_t value, int64_t* old_value);
 

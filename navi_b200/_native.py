@@ -70,8 +70,8 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_pool_load": (c_int, [c_char_p, c_int, ctypes.POINTER(c_void_p)]),
     "tsdf_pool_destroy": (c_int, [c_void_p]),
     "tsdf_pool_stats_get": (c_int, [c_void_p, ctypes.POINTER(PoolStats)]),
-    "tsdf_fan_workspace_bytes": (c_uint64, [c_int64]),
-    "tsdf_workspace_bytes": (c_uint64, []),
+    "tsdf_fan_workspace_bytes": (c_uint64, [c_void_p, c_int64, c_int64]),
+    "tsdf_workspace_bytes": (c_uint64, [c_int64]),
     "tsdf_cast": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                           c_float, ctypes.POINTER(c_float), ctypes.POINTER(c_float), c_float, c_void_p, c_void_p]),
     "tsdf_scenes_create": (c_int, [ctypes.POINTER(c_void_p), c_int, ctypes.POINTER(c_float), ctypes.POINTER(c_float),
@@ -80,7 +80,7 @@ TSDF_SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tsdf_cast_fan": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                               c_int, c_float, c_void_p, c_void_p]),
     "tsdf_set_option": (c_int, [c_char_p, c_int64, ctypes.POINTER(c_int64)]),
-    "tsdf_observe_workspace_bytes": (c_uint64, [c_int64]),
+    "tsdf_observe_workspace_bytes": (c_uint64, [c_void_p, c_int64, c_int64]),
     "tsdf_cast_fan_observe": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p,
                                       c_void_p, c_int, c_float, ctypes.POINTER(Observe), c_void_p, c_void_p]),
     "tsdf_cast_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,

@@ -271,7 +271,6 @@ const char* tsdf_last_error(void) { return tsdf::last_error_cstr(); }
 
 int tsdf_version(void) { return TSDF_ABI_VERSION; }
 
-uint64_t tsdf_workspace_bytes(void) { return 256; }
 
 static int check_device(int device)
 {

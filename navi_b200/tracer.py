@@ -67,9 +67,9 @@ def _stream_handle(device: torch.device) -> int:
     return int(torch.cuda.current_stream(device).cuda_stream)
 
 
-def workspace(device: torch.device) -> torch.Tensor:
-    """Scratch for one cast (a work counter), allocated on the current stream."""
-    n = int(_native.tsdf_lib().tsdf_workspace_bytes())
+def workspace(device: torch.device, n_rays: int) -> torch.Tensor:
+    """Scratch for one cast of n_rays rays (work counter, claim order), allocated on the current stream."""
+    n = int(_native.tsdf_lib().tsdf_workspace_bytes(int(n_rays)))
     return torch.empty(n, dtype=torch.uint8, device=device)
 
 
@@ -247,7 +247,7 @@ def cast_rays_ex(
     if out_steps is not None and (out_steps.numel() != n or out_steps.dtype != torch.int32 or not out_steps.is_contiguous()):
         raise RuntimeError("out_steps must be a contiguous int32 tensor with one entry per ray")
     _same_device(pool.device, origins, dirs, out_distances, out_semantics, out_steps)
-    ws = workspace(pool.device)
+    ws = workspace(pool.device, n)
     lib = _native.tsdf_lib()
     with _nvtx("tsdf_cast"):
         rc = lib.tsdf_cast(
@@ -421,7 +421,7 @@ def cast_fan(
         raise RuntimeError("out_steps must be a contiguous int32 tensor of actors x rays entries")
     _same_device(scenes.device, poses, fan_dirs, out_distances, out_semantics, out_steps)
     lib = _native.tsdf_lib()
-    ws = torch.empty(int(lib.tsdf_fan_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
+    ws = torch.empty(int(lib.tsdf_fan_workspace_bytes(scenes.handle, a, r)), dtype=torch.uint8, device=scenes.device)
     with _nvtx("tsdf_cast_fan"):
         rc = lib.tsdf_cast_fan(
             scenes.handle, ctypes.c_void_p(poses.data_ptr()), a, ctypes.c_void_p(fan_dirs.data_ptr()), r,
@@ -472,7 +472,7 @@ def cast_fan_observe(
         raise RuntimeError("out_steps must be a contiguous int32 tensor of actors x rays entries")
     _same_device(scenes.device, poses, fan_dirs, out_distances, out_semantics, observation, actor_stats, out_steps)
     lib = _native.tsdf_lib()
-    ws = torch.empty(int(lib.tsdf_observe_workspace_bytes(a)), dtype=torch.uint8, device=scenes.device)
+    ws = torch.empty(int(lib.tsdf_observe_workspace_bytes(scenes.handle, a, r)), dtype=torch.uint8, device=scenes.device)
     ob = _native.Observe(int(azimuth_bins), int(elevation_bins), float(structure_band_min), float(structure_band_max),
                          float(proximity_threshold), observation.data_ptr(), actor_stats.data_ptr())
     with _nvtx("tsdf_cast_fan_observe"):

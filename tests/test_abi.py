@@ -37,7 +37,13 @@ def test_library_exports_every_declared_symbol():
 def test_version_and_workspace_query():
     lib = _native.tsdf_lib()
     assert lib.tsdf_version() == 1
-    assert lib.tsdf_workspace_bytes() >= 4
+    assert lib.tsdf_workspace_bytes(0) >= 8
+    # counter block + 128 bucket words + 4-byte order + 1-byte key per ray, rounded to 16
+    assert lib.tsdf_workspace_bytes(1000) == 256 + 512 + 4000 + 1008
+    assert lib.tsdf_fan_workspace_bytes(None, 10, 0) == 256
+    assert lib.tsdf_fan_workspace_bytes(None, 10, 100) == 256 + 512 + 4000 + 1008
+    assert lib.tsdf_fan_workspace_bytes(None, 4096, 1) == 256 + 512 + 5 * 4096
+    assert lib.tsdf_observe_workspace_bytes(None, 10, 100) == lib.tsdf_fan_workspace_bytes(None, 10, 100)
 
 
 def test_option_knobs_validate_their_range():
@@ -47,6 +53,8 @@ def test_option_knobs_validate_their_range():
     assert lib.tsdf_set_option(b"chunk", old.value, None) == 0
     assert lib.tsdf_set_option(b"chunk", 0, None) != 0
     assert b"chunk" in lib.tsdf_last_error()
+    assert lib.tsdf_set_option(b"order", 2, None) != 0
+    assert b"order" in lib.tsdf_last_error()
     assert lib.tsdf_set_option(b"no_such_knob", 1, None) != 0
     assert b"unknown option" in lib.tsdf_last_error()
 

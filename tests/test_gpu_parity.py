@@ -493,7 +493,8 @@ def test_multiscene_actor_with_unknown_scene_is_not_traced(descent):
 
 @pytest.mark.parametrize("opts", [
     {"smem_records": 1024}, {"smem_records": 37}, {"leaf_run": 0}, {"leaf_run": 8}, {"chunk": 1},
-    {"chunk": 64}, {"blocks_per_sm": 1}, {"smem_records": 1024, "leaf_run": 3, "chunk": 3, "blocks_per_sm": 2},
+    {"chunk": 64}, {"blocks_per_sm": 1}, {"order": 0},
+    {"smem_records": 1024, "leaf_run": 3, "chunk": 3, "blocks_per_sm": 2, "order": 0},
 ])
 def test_tuning_options_do_not_change_results(opts):
     """Every knob of tsdf_set_option changes scheduling only: single- and multi-scene fan
@@ -535,6 +536,47 @@ def test_tuning_options_do_not_change_results(opts):
         assert_bits_equal(gd, wd, f"dist under {opts}")
         assert_equal(gs, ws, f"sem under {opts}")
         assert_equal(gk, wk, f"steps under {opts}")
+
+
+@pytest.mark.parametrize("n", [1, 2047, 2048, 2049, 3 * 2048 + 5, 70001])
+def test_claim_order_traces_every_ray_once(n):
+    """Single-scene launches claim rays longest scene-box exit first, through a bucket
+    order built on the device (per-block ranks, one reservation per bucket and block).
+    Every ray must be traced exactly once whatever the bucket mix: sentinel-prefilled
+    outputs under the default order equal index order bit for bit and the oracle.  The
+    rays mix one crowded bucket (copies of one ray), rays that start outside the box and
+    leave it, and random rays, over sizes around the 2048-ray scatter tile."""
+    cfg = scenes.CONFIGS[1]
+    cs = workloads.compiled_scene(1)
+    rng = np.random.default_rng(n)
+    origins = rng.uniform(0.5, 9.5, size=(n, 3)).astype(np.float32)
+    dirs = rng.normal(size=(n, 3)).astype(np.float32)
+    dirs /= np.linalg.norm(dirs, axis=1, keepdims=True)
+    third = n // 3
+    origins[:third] = origins[0]
+    dirs[:third] = dirs[0]
+    out = slice(third, third + n // 4)
+    origins[out] = np.array([-3.0, 5.0, 5.0], np.float32)
+    dirs[out] = np.array([-1.0, 0.0, 0.0], np.float32)
+    kw = dict(max_steps=cfg.max_steps, max_distance=cfg.max_distance, bbox_min=cs.bbox_min, bbox_max=cs.bbox_max,
+              hit_epsilon=cs.hit_epsilon)
+    pool = tracer.NodePool.from_words(cs.words, dev())
+    ordered = cast_explicit(cs.words, origins, dirs, pool=pool, **kw)
+    old = tracer.set_option("order", 0)
+    try:
+        plain = cast_explicit(cs.words, origins, dirs, pool=pool, **kw)
+    finally:
+        tracer.set_option("order", old)
+    assert np.all(ordered[2] >= 0), "a ray was left untraced"
+    assert_bits_equal(ordered[0], plain[0], "dist")
+    assert_equal(ordered[1], plain[1], "sem")
+    assert_equal(ordered[2], plain[2], "steps")
+    pick = np.unique(np.concatenate([np.arange(min(n, 64)), rng.integers(0, n, size=min(n, 512))]))
+    ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, origins[pick], dirs[pick], max_steps=cfg.max_steps,
+                  max_distance=cfg.max_distance, hit_epsilon=cs.hit_epsilon)
+    assert_bits_equal(ordered[0][pick], ref["dist"], "dist vs oracle")
+    assert_equal(ordered[1][pick], ref["sem"], "sem vs oracle")
+    assert_equal(ordered[2][pick], ref["steps"], "steps vs oracle")
 
 
 @pytest.mark.parametrize("az,el,actors", [(1, 1, 5), (17, 5, 9), (255, 47, 3), (3, 1, 700)])

@@ -51,11 +51,11 @@ def test_noalloc_cast_matches_tsdf_cast_on_consecutive_calls():
     try:
         f3 = ctypes.c_float * 3
         bmin, bmax = f3(*cs.bbox_min), f3(*cs.bbox_max)
-        ws = torch.zeros(int(lib.tsdf_workspace_bytes()), dtype=torch.uint8, device=dev)
         stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
         for call, seed in enumerate((11, 12)):
             _, o, d = _rays(1, seed, dev)
             n = o.shape[0]
+            ws = torch.zeros(int(lib.tsdf_workspace_bytes(n)), dtype=torch.uint8, device=dev)
             outs = []
             for which in ("noalloc", "workspace"):
                 od = torch.full((n,), -7.0, dtype=torch.float32, device=dev)
