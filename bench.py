@@ -523,9 +523,9 @@ def _traffic(workload: str):
 
 
 def _observe(torch, tracer, args, cfg, sset, poses, fan, use_pitch, flush, dev, scene_list) -> dict:
-    """Cast with the reference's post-processing fused into the kernel (observation [A,3,Az,El]
-    + per-actor ratios).  The reference's own post-processing (eager torch ops after the cast)
-    is timed by the --impl reference arm."""
+    """Cast followed by the reference's post-processing as one pass over its outputs
+    (observation [A,3,Az,El] + per-actor ratios).  The reference's own post-processing
+    (eager torch ops after the cast) is timed by the --impl reference arm."""
     a, r = poses.shape[0], fan.shape[0]
     az, el = cfg.azimuth_bins, cfg.elevation_bins
     band = _band(scene_list)
