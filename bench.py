@@ -491,9 +491,10 @@ def run_navi(args) -> None:
                 "pool_bytes": int(sum(p.stats["device_bytes"] for p in pools)),
                 "descent": args.descent,
             },
-            # per step: the trace kernel, plus the scene-order sort for scene tables of more than one
-            # scene, or the claim-order key and scatter kernels for one scene
-            "gpu_launches": args.steps * (2 if len(scene_list) > 1 else 3),
+            # per step: one scene: the claim-order key and scatter kernels and the trace kernel;
+            # 2-64 scenes: the scene sort, one trace launch per scene and the unknown-scene fill
+            "gpu_launches": args.steps * (3 if len(scene_list) == 1 else
+                                          (len(scene_list) + 2 if len(scene_list) <= 64 else 2)),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "e2e_fan": e2e_fan,

@@ -139,7 +139,8 @@ TSDF_API int tsdf_scenes_destroy(tsdf_scenes* scenes);
 /* Device bytes of workspace tsdf_cast_fan needs for n_actors x rays_per_actor rays
  * on `scenes`: the work counter and, for a table of one scene, the claim order (as
  * tsdf_workspace_bytes), for more than one scene the actor order by scene (4 bytes
- * per actor).  scenes = NULL gives the larger of the two. */
+ * per actor, rounded up to 16) and 1 KB of per-scene bounds and counters.
+ * scenes = NULL gives the larger of the two. */
 TSDF_API uint64_t tsdf_fan_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors,
                                            int64_t rays_per_actor);
 
@@ -211,7 +212,9 @@ TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, cons
  * "descent" (0 = integer grid descent wherever the DAG allows it, 1 = float
  * descent only), "order" (single-scene claim order: 1 = rays that can travel
  * farthest inside the scene box are claimed first, the default; 0 = ray index
- * order).  No knob changes results.  Returns the old value through
+ * order), "per_scene" (scene tables of 2 to 64 scenes: 1 = one single-scene launch
+ * per scene over the actors sorted by scene on the device, the default; 0 = one
+ * multi-scene launch).  No knob changes results.  Returns the old value through
  * *old_value when not NULL. */
 TSDF_API int tsdf_set_option(const char* key, int64_t value, int64_t* old_value);
 

@@ -74,6 +74,8 @@ struct TraceArgs {
     uint32_t leaf_run;           // leaf-cache steps taken in place after a step (grid kernel)
     const uint32_t* perm;        // multi-scene fan launches: actors in scene order (or null)
     const uint32_t* ray_perm;    // single-scene launches: rays in claim order (or null)
+    const uint32_t* seg;         // per-scene launch of a scene table: its actors are perm[seg[0], seg[1])
+                                 // (device, written by scene_sort_kernel), or null
     uint32_t n_scenes;           // multi-scene fan launches: scene table size
     float* out_d;
     int32_t* out_s;
@@ -153,8 +155,16 @@ __device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3&
 // scene and the SM's L1 holds the hot records and grid lines of fewer scenes; outputs
 // stay actor-major.  The traced values do not depend on the order.
 template <bool kFan, bool kMulti>
-__device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w)
+__device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w, uint32_t seg_base)
 {
+    if constexpr (kFan && !kMulti) {
+        if (a.seg) {
+            const uint32_t slot = div_rpa(a, w);
+            uint32_t actor = __ldg(a.perm + seg_base + slot);
+            if (!checked(a.err, actor < a.n_rays / a.rays_per_actor, kErrActor)) actor = 0;
+            return actor * a.rays_per_actor + (w - slot * a.rays_per_actor);
+        }
+    }
     if constexpr (!kMulti) {
         if (a.ray_perm) {
             const uint32_t r = __ldg(a.ray_perm + w);
@@ -174,9 +184,11 @@ __device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w)
 
 // Counting sort of the actors by scene index, one block: perm[i] = the i-th actor in
 // scene order (scenes ascending, actors of one scene in arbitrary order; indices outside
-// [0, n_scenes) last).
+// [0, n_scenes) last).  seg (may be null) receives the n_scenes + 2 bounds: scene b's
+// actors are perm[seg[b], seg[b + 1]), those of no scene perm[seg[n_scenes], n_actors).
 __global__ void __launch_bounds__(1024) scene_sort_kernel(const float4* __restrict__ poses, uint32_t n_actors,
-                                                          uint32_t n_scenes, uint32_t* __restrict__ perm)
+                                                          uint32_t n_scenes, uint32_t* __restrict__ perm,
+                                                          uint32_t* __restrict__ seg)
 {
     extern __shared__ unsigned int bucket[];  // [n_scenes + 1]
     for (uint32_t i = threadIdx.x; i <= n_scenes; i += blockDim.x) bucket[i] = 0;
@@ -191,13 +203,37 @@ __global__ void __launch_bounds__(1024) scene_sort_kernel(const float4* __restri
         for (uint32_t b = 0; b <= n_scenes; ++b) {
             const unsigned int c = bucket[b];
             bucket[b] = run;
+            if (seg) seg[b] = run;
             run += c;
         }
+        if (seg) seg[n_scenes + 1] = run;
     }
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < n_actors; i += blockDim.x) {
         const uint32_t sc = static_cast<uint32_t>(__float_as_int(__ldg(poses + 2 * static_cast<size_t>(i) + 1).w));
         perm[atomicAdd(&bucket[sc < n_scenes ? sc : n_scenes], 1u)] = i;
+    }
+}
+
+// Rays of the actors whose scene index is outside the table, in a per-scene traced
+// scene table: not traced (NaN distance, semantic 0, 0 steps), as the multi-scene kernel
+// leaves them.  seg points at the bounds [seg[0], seg[1]) of those actors in perm.
+__global__ void __launch_bounds__(256) unknown_scene_kernel(const uint32_t* __restrict__ seg,
+                                                            const uint32_t* __restrict__ perm, uint32_t n_actors,
+                                                            uint32_t rays_per_actor, float* __restrict__ out_d,
+                                                            int32_t* __restrict__ out_s, int32_t* __restrict__ out_steps)
+{
+    const uint32_t lo = __ldg(seg), hi = min(__ldg(seg + 1), n_actors);
+    if (lo >= hi) return;
+    const uint64_t n = static_cast<uint64_t>(hi - lo) * rays_per_actor;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t actor = __ldg(perm + lo + i / rays_per_actor);
+        if (actor >= n_actors) continue;
+        const uint64_t ray = static_cast<uint64_t>(actor) * rays_per_actor + i % rays_per_actor;
+        out_d[ray] = __int_as_float(0x7fc00000);
+        out_s[ray] = 0;
+        if (out_steps) out_steps[ray] = 0;
     }
 }
 
@@ -361,6 +397,16 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
         for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
         __syncthreads();
     }
+    // per-scene launch of a scene table: the scene's actor range, read once
+    uint32_t seg_base = 0, n_work = a.n_rays;
+    if constexpr (kFan && !kMulti) {
+        if (a.seg) {
+            seg_base = __ldg(a.seg);
+            const uint32_t seg_end = __ldg(a.seg + 1);
+            const bool ok = checked(a.err, seg_base <= seg_end && seg_end <= a.n_rays / a.rays_per_actor, kErrActor);
+            n_work = ok ? (seg_end - seg_base) * a.rays_per_actor : 0u;
+        }
+    }
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t lt_mask = (1u << lane) - 1u;
 
@@ -406,18 +452,18 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
                 uint32_t base = 0;
                 if (lane == 0) base = atomicAdd(a.counter, a.chunk);
                 base = __shfl_sync(kFull, base, 0);
-                if (base >= a.n_rays) {
+                if (base >= n_work) {
                     exhausted = true;
                 } else {
                     q_next = base;
-                    q_end = min(base + a.chunk, a.n_rays);
+                    q_end = min(base + a.chunk, n_work);
                     const uint32_t got = min(nidle - take, q_end - q_next);
                     if (!active && rank >= take && rank - take < got) mine = q_next + (rank - take);
                     q_next += got;
                 }
             }
             if (mine != 0xFFFFFFFFu) {
-                ray = work_ray<kFan, kMulti>(a, mine);
+                ray = work_ray<kFan, kMulti>(a, mine, seg_base);
                 active = true;
                 t = 0.f;
                 dist = 0.f;
@@ -883,6 +929,16 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
         }
     }
 
+    // per-scene launch of a scene table: the scene's actor range, read once
+    uint32_t seg_base = 0, n_work = a.n_rays;
+    if constexpr (kFan && !kMulti) {
+        if (a.seg) {
+            seg_base = __ldg(a.seg);
+            const uint32_t seg_end = __ldg(a.seg + 1);
+            const bool ok = checked(a.err, seg_base <= seg_end && seg_end <= a.n_rays / a.rays_per_actor, kErrActor);
+            n_work = ok ? (seg_end - seg_base) * a.rays_per_actor : 0u;
+        }
+    }
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* my_stack = s_stack + threadIdx.x;
     uint32_t q_next = 0, q_end = 0;
@@ -902,10 +958,10 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
     uint32_t pre_rec = 0, node = 0;
 
     for (;;) {
-        const uint32_t mine = claim_ray(q_next, q_end, exhausted, active, lane, a.counter, a.chunk, a.n_rays);
+        const uint32_t mine = claim_ray(q_next, q_end, exhausted, active, lane, a.counter, a.chunk, n_work);
         if (mine != 0xFFFFFFFFu) {
             int scene = 0;
-            ray = work_ray<kFan, kMulti>(a, mine);
+            ray = work_ray<kFan, kMulti>(a, mine, seg_base);
             load_ray<kFan>(a, ray, o, d, scene);
             active = true;
             t = 0.f;
@@ -1139,7 +1195,8 @@ uint64_t order_scratch_bytes(int64_t n_rays)
 constexpr int64_t kSmemReservedPerBlock = 1024;  // shared memory the driver reserves per resident block
 
 template <bool kFan, bool kMulti>
-int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream, bool order = true)
+int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream, bool order = true,
+           unsigned int* counter = nullptr)
 {
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
@@ -1187,11 +1244,15 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     }
     const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
     const int blocks = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(sms) * per_sm, need));
-    a.counter = static_cast<unsigned int*>(workspace);
-    a.err = a.counter + 1;
-    const size_t clear = 2 * sizeof(unsigned int);
-    e = cudaMemsetAsync(workspace, 0, clear, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    if (counter) {
+        a.counter = counter;  // cleared by the caller
+        a.err = counter + 1;
+    } else {
+        a.counter = static_cast<unsigned int*>(workspace);
+        a.err = a.counter + 1;
+        e = cudaMemsetAsync(workspace, 0, 2 * sizeof(unsigned int), stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+    }
     if constexpr (!kMulti) {
         // claim order into the workspace after the counter: bucket counts and cursors,
         // the order itself, the per-ray bucket keys
@@ -1258,7 +1319,8 @@ bool pool_grid_ok(tsdf_pool* pool, const float* bmin, const float* bmax)
 // (4 bytes per actor of the caller's workspace), on `stream` before the trace.
 constexpr uint32_t kMaxSortedScenes = 8192;  // shared-memory buckets of the sort
 
-int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, void* perm_mem, cudaStream_t stream)
+int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, void* perm_mem, cudaStream_t stream,
+                  uint32_t* seg = nullptr)
 {
     a.n_scenes = static_cast<uint32_t>(scenes->n);
     a.perm = nullptr;
@@ -1268,7 +1330,7 @@ int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, voi
     auto* perm = static_cast<uint32_t*>(perm_mem);
     const size_t smem = (static_cast<size_t>(scenes->n) + 1) * sizeof(unsigned int);
     scene_sort_kernel<<<1, 1024, smem, stream>>>(a.poses, static_cast<uint32_t>(n_actors),
-                                                 static_cast<uint32_t>(scenes->n), perm);
+                                                 static_cast<uint32_t>(scenes->n), perm, seg);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "scene sort launch");
     a.perm = perm;
@@ -1290,6 +1352,114 @@ uint32_t clamp_chunk()
 {
     const int64_t c = g_chunk.load();
     return static_cast<uint32_t>(c < 1 ? 1 : (c > 1024 ? 1024 : c));
+}
+
+// Scene tables of up to kMaxPerSceneLaunch scenes trace one single-scene launch per
+// scene (option "per_scene", default 1) instead of the multi-scene kernel: each launch
+// keeps its scene in uniform parameters and its grid lines in shared memory and takes
+// leaf runs, which the multi-scene kernel cannot (on config 3's actors all in one scene
+// the multi-scene kernel is 12% slower than the single-scene one).  The actor order by
+// scene and each scene's actor range come from scene_sort_kernel on the device, so the
+// host needs no counts: every launch reads its range at start and exits at once when it
+// is empty.  Workspace after the actor order: the scene bounds, then a work counter and
+// error word per launch.
+constexpr int kMaxPerSceneLaunch = 64;
+constexpr size_t kPerSceneBytes = 1024;  // (kMaxPerSceneLaunch + 2) bounds + 2 words per launch
+static_assert((kMaxPerSceneLaunch + 2) * 4 + kMaxPerSceneLaunch * 8 <= kPerSceneBytes, "per-scene workspace");
+std::atomic<int64_t> g_per_scene{1};
+
+size_t actor_order_bytes(int64_t n_actors)
+{
+    return (static_cast<size_t>(n_actors) * 4u + 15u) & ~size_t(15);
+}
+
+bool per_scene_launches(const tsdf_scenes* scenes)
+{
+    return scenes->n > 1 && scenes->n <= kMaxPerSceneLaunch && g_per_scene.load() != 0;
+}
+
+// Library streams that per-scene launches alternate on, so that a launch's blocks fill
+// the SMs the previous launch frees as its last rays finish (one pair per device, made
+// on first use; the caller's stream forks to them and joins back through events, which
+// stream capture follows).
+constexpr int kPerSceneStreams = 2;
+struct SceneStreams {
+    cudaStream_t s[kPerSceneStreams] = {};
+    cudaEvent_t fork = nullptr;
+    cudaEvent_t join[kPerSceneStreams] = {};
+    bool ready = false;
+    std::mutex mu;  // one call at a time between fork and join: the events are shared
+};
+constexpr int kMaxStreamDevices = 64;
+std::mutex g_streams_mu;
+SceneStreams g_streams[kMaxStreamDevices];
+
+SceneStreams* scene_streams(int device)
+{
+    if (device < 0 || device >= kMaxStreamDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_streams_mu);
+    SceneStreams& st = g_streams[device];
+    if (!st.ready) {
+        bool ok = cudaEventCreateWithFlags(&st.fork, cudaEventDisableTiming) == cudaSuccess;
+        for (int i = 0; i < kPerSceneStreams && ok; ++i)
+            ok = cudaStreamCreateWithFlags(&st.s[i], cudaStreamNonBlocking) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&st.join[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            return nullptr;  // the launches stay on the caller's stream
+        }
+        st.ready = true;
+    }
+    return &st;
+}
+
+int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, void* workspace, cudaStream_t stream)
+{
+    char* ws = static_cast<char*>(workspace);
+    auto* seg = reinterpret_cast<uint32_t*>(ws + kScratchOffset + actor_order_bytes(n_actors));
+    auto* counters = seg + (kMaxPerSceneLaunch + 2);
+    int rc = sort_by_scene(a, scenes, n_actors, ws + kScratchOffset, stream, seg);
+    if (rc != TSDF_OK) return rc;
+    cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned int) * scenes->n, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(per-scene counters)");
+    const bool grid_ok = g_descent.load() == 0;
+    SceneStreams* st = scene_streams(scenes->device);
+    std::unique_lock<std::mutex> hold;
+    if (st) hold = std::unique_lock<std::mutex>(st->mu);
+    if (st) {
+        e = cudaEventRecord(st->fork, stream);
+        for (int i = 0; i < kPerSceneStreams && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(st->s[i], st->fork, 0);
+        if (e != cudaSuccess) return cuda_fail(e, "forking the per-scene streams");
+    }
+    for (int s = 0; s < scenes->n; ++s) {
+        TraceArgs b = a;
+        b.table = nullptr;
+        b.n_scenes = 0;
+        b.scene = scenes->host[s];
+        b.seg = seg + s;
+        b.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
+                                                           static_cast<int64_t>(b.scene.n_recs)));
+        const bool grid = grid_ok && b.scene.depth >= 0;
+        if (!grid) b.scene.depth = -1;
+        rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, b, scenes->device, workspace,
+                                 st ? st->s[s % kPerSceneStreams] : stream, /*order=*/false, counters + 2 * s);
+        if (rc != TSDF_OK) return rc;
+    }
+    if (st) {
+        for (int i = 0; i < kPerSceneStreams && e == cudaSuccess; ++i) {
+            e = cudaEventRecord(st->join[i], st->s[i]);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, st->join[i], 0);
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "joining the per-scene streams");
+    }
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scenes->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    unknown_scene_kernel<<<static_cast<unsigned>(sms), 256, 0, stream>>>(
+        seg + scenes->n, a.perm, static_cast<uint32_t>(n_actors), a.rays_per_actor, a.out_d, a.out_s, a.out_steps);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "unknown-scene launch");
+    return TSDF_OK;
 }
 
 }  // namespace
@@ -1388,6 +1558,7 @@ int tsdf_cast_fan(const tsdf_scenes* scenes, const tsdf_pose* poses, int64_t n_a
     }
     a.table = scenes->d_table;
     a.scene = scenes->host[0];
+    if (per_scene_launches(scenes)) return trace_per_scene(a, scenes, n_actors, workspace, static_cast<cudaStream_t>(stream));
     rc = sort_by_scene(a, scenes, n_actors, static_cast<char*>(workspace) + kScratchOffset,
                        static_cast<cudaStream_t>(stream));
     if (rc != TSDF_OK) return rc;
@@ -1403,7 +1574,7 @@ uint64_t tsdf_workspace_bytes(int64_t n_rays)
 uint64_t tsdf_fan_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors, int64_t rays_per_actor)
 {
     if (n_actors <= 0 || rays_per_actor <= 0) return kScratchOffset;
-    const uint64_t by_scene = static_cast<uint64_t>(n_actors) * 4u;
+    const uint64_t by_scene = actor_order_bytes(n_actors) + kPerSceneBytes;
     const uint64_t order = order_scratch_bytes(n_actors * rays_per_actor);
     if (!scenes) return kScratchOffset + std::max(by_scene, order);
     return kScratchOffset + (scenes->n > 1 ? by_scene : order);
@@ -1480,6 +1651,10 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
         const bool grid = scenes->grid && g_descent.load() == 0;
         if (!grid) a.scene.depth = -1;
         rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, a, scenes->device, workspace, s);
+    } else if (per_scene_launches(scenes)) {
+        a.table = scenes->d_table;
+        a.scene = scenes->host[0];
+        rc = trace_per_scene(a, scenes, n_actors, workspace, s);
     } else {
         a.table = scenes->d_table;
         a.scene = scenes->host[0];
@@ -1511,6 +1686,9 @@ int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
     } else if (std::strcmp(key, "leaf_run") == 0) {
         if (value < 0 || value > 4096) return fail(TSDF_ERR_INVALID, "leaf_run must be in [0, 4096]");
         slot = &g_leaf_run;
+    } else if (std::strcmp(key, "per_scene") == 0) {
+        if (value < 0 || value > 1) return fail(TSDF_ERR_INVALID, "per_scene must be 0 or 1");
+        slot = &g_per_scene;
     } else if (std::strcmp(key, "order") == 0) {
         if (value < 0 || value > 1) return fail(TSDF_ERR_INVALID, "order must be 0 or 1");
         slot = &g_order;

@@ -55,6 +55,8 @@ def test_option_knobs_validate_their_range():
     assert b"chunk" in lib.tsdf_last_error()
     assert lib.tsdf_set_option(b"order", 2, None) != 0
     assert b"order" in lib.tsdf_last_error()
+    assert lib.tsdf_set_option(b"per_scene", 2, None) != 0
+    assert b"per_scene" in lib.tsdf_last_error()
     assert lib.tsdf_set_option(b"no_such_knob", 1, None) != 0
     assert b"unknown option" in lib.tsdf_last_error()
 

@@ -493,7 +493,7 @@ def test_multiscene_actor_with_unknown_scene_is_not_traced(descent):
 
 @pytest.mark.parametrize("opts", [
     {"smem_records": 1024}, {"smem_records": 37}, {"leaf_run": 0}, {"leaf_run": 8}, {"chunk": 1},
-    {"chunk": 64}, {"blocks_per_sm": 1}, {"order": 0},
+    {"chunk": 64}, {"blocks_per_sm": 1}, {"order": 0}, {"per_scene": 0}, {"per_scene": 0, "leaf_run": 0},
     {"smem_records": 1024, "leaf_run": 3, "chunk": 3, "blocks_per_sm": 2, "order": 0},
 ])
 def test_tuning_options_do_not_change_results(opts):
