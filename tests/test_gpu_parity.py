@@ -494,6 +494,7 @@ def test_multiscene_actor_with_unknown_scene_is_not_traced(descent):
 @pytest.mark.parametrize("opts", [
     {"smem_records": 1024}, {"smem_records": 37}, {"leaf_run": 0}, {"leaf_run": 8}, {"chunk": 1},
     {"chunk": 64}, {"blocks_per_sm": 1}, {"order": 0}, {"per_scene": 0}, {"per_scene": 0, "leaf_run": 0},
+    {"descent": 1},
     {"smem_records": 1024, "leaf_run": 3, "chunk": 3, "blocks_per_sm": 2, "order": 0},
 ])
 def test_tuning_options_do_not_change_results(opts):
@@ -693,3 +694,80 @@ def test_config5_step_sampled_oracle_and_determinism():
     assert_bits_equal(outs[0][0], outs[1][0], "repeat dist")
     assert_equal(outs[0][2], outs[1][2], "repeat steps")
     _sampled_oracle_check(cfg, scene_list, pb, fan, *outs[0], 200_000, 5)
+
+
+@pytest.mark.parametrize("n_scenes", [2, 64, 65])
+def test_scene_tables_per_scene_launches_and_multi_scene_kernel(n_scenes):
+    """Scene tables of 2 and 64 scenes take one single-scene launch per scene (actor
+    ranges from the device scene sort, launches alternating on two library streams); 65
+    scenes take the multi-scene kernel.  Random DAGs of depths 1-5 in non-cubic boxes
+    (one cyclic DAG, traced by the float descent, in tables of 3+ scenes), a scene with
+    no actors, and actors whose scene index is outside the table: the outputs equal the
+    multi-scene kernel's bit for bit and the oracle on each actor's explicit rays;
+    actors of no scene get NaN distance, semantic 0 and 0 steps."""
+    from navi_b200.fan import build_spherical_ray_directions
+    from tests.dag_fuzz import random_dag
+    from tests.kat_cases import leaf_word
+
+    rng = np.random.default_rng(500 + n_scenes)
+    dags, bmins, bmaxs, eps = [], [], [], []
+    for i in range(n_scenes):
+        if i == 2:
+            dags.append(np.array([internal_word_(0b10000001, 1), 0, 3, leaf_word(0.003, 2)], np.uint64))
+        else:
+            dags.append(random_dag(rng, int(rng.integers(1, 6))))
+        lo = rng.uniform(-2.0, 0.0, size=3).astype(np.float32)
+        bmins.append(tuple(float(x) for x in lo))
+        bmaxs.append(tuple(float(x) for x in lo + rng.uniform(0.5, 3.0, size=3).astype(np.float32)))
+        eps.append(float(rng.choice([0.01, 0.05, 0.2])))
+    sset = tracer.SceneSet([tracer.NodePool.from_words(w, dev()) for w in dags], bmins, bmaxs, eps)
+    actors = 3 * n_scenes + 5
+    scene = rng.integers(0, n_scenes, size=actors).astype(np.int32)
+    scene[scene == 1] = 0                       # scene 1 has no actors
+    scene[rng.choice(actors, size=4, replace=False)] = [n_scenes, n_scenes + 3, -1, 1 << 20]
+    pos = np.empty((actors, 3), np.float32)
+    for a in range(actors):
+        s = scene[a] if 0 <= scene[a] < n_scenes else 0
+        lo, hi = np.array(bmins[s], np.float32), np.array(bmaxs[s], np.float32)
+        pos[a] = lo + rng.uniform(0.05, 0.95, size=3).astype(np.float32) * (hi - lo)
+    yaw = rng.uniform(-np.pi, np.pi, size=actors).astype(np.float32)
+    pitch = rng.uniform(-0.3, 0.3, size=actors).astype(np.float32)
+    poses = tracer.make_poses(torch.from_numpy(pos).to(dev()), torch.from_numpy(yaw).to(dev()),
+                              torch.from_numpy(pitch).to(dev()), torch.from_numpy(scene).to(dev()))
+    fan = torch.from_numpy(build_spherical_ray_directions(9, 3)).to(dev())
+    r = fan.shape[0]
+    kw = dict(max_steps=48, max_distance=5.0, use_pitch=True)
+
+    def run():
+        d = torch.full((actors * r,), -7.0, device=dev())
+        s = torch.full((actors * r,), -7, dtype=torch.int32, device=dev())
+        k = torch.full((actors * r,), -7, dtype=torch.int32, device=dev())
+        tracer.cast_fan(sset, poses, fan, d, s, out_steps=k, **kw)
+        torch.cuda.synchronize()
+        return d.cpu().numpy().reshape(actors, r), s.cpu().numpy().reshape(actors, r), k.cpu().numpy().reshape(actors, r)
+
+    got = run()
+    old = tracer.set_option("per_scene", 0)
+    try:
+        multi = run()
+    finally:
+        tracer.set_option("per_scene", old)
+    for g, m, what in zip(got, multi, ("dist", "sem", "steps")):
+        if what == "dist":
+            assert_bits_equal(g, m, "dist vs multi-scene kernel")
+        else:
+            assert_equal(g, m, f"{what} vs multi-scene kernel")
+    o, v = eager_world_rays(fan, poses, pitch=True)
+    o, v = o.cpu().numpy(), v.cpu().numpy()
+    for s in range(n_scenes):
+        sel = np.nonzero(scene == s)[0]
+        if sel.size == 0:
+            continue
+        ref = O.trace(dags[s], bmins[s], bmaxs[s], o[sel].reshape(-1, 3), v[sel].reshape(-1, 3),
+                      max_steps=48, max_distance=5.0, hit_epsilon=eps[s])
+        assert_bits_equal(got[0][sel].reshape(-1), ref["dist"], f"scene {s} dist")
+        assert_equal(got[1][sel].reshape(-1), ref["sem"], f"scene {s} sem")
+        assert_equal(got[2][sel].reshape(-1), ref["steps"], f"scene {s} steps")
+    bad = np.nonzero((scene < 0) | (scene >= n_scenes))[0]
+    assert bad.size == 4
+    assert np.all(np.isnan(got[0][bad])) and np.all(got[1][bad] == 0) and np.all(got[2][bad] == 0)
