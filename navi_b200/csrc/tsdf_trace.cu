@@ -15,7 +15,11 @@
 // step if it finished.  Lanes whose ray has ended are refilled at the top of
 // the next iteration from a warp-local range of ray indices; the warp claims
 // ranges of `chunk` rays from a global counter with one atomicAdd, so short
-// rays never leave lanes idle while long rays march on.
+// rays never leave lanes idle while long rays march on.  Around the trace:
+// the claim order of single-scene launches (order_key_kernel,
+// order_scatter_kernel), the scene sort of scene tables (scene_sort_kernel;
+// tables of 2-64 scenes then take one single-scene launch per scene, larger
+// ones the multi-scene kernel) and the observation pass (observe_kernel).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -152,8 +156,10 @@ __device__ __forceinline__ void load_ray(const TraceArgs& a, uint32_t r, float3&
 
 // Work item w -> output ray.  Multi-scene fan launches take actors grouped by scene
 // (perm, written by scene_sort_kernel), so that the warps of a block mostly trace one
-// scene and the SM's L1 holds the hot records and grid lines of fewer scenes; outputs
-// stay actor-major.  The traced values do not depend on the order.
+// scene and the SM's L1 holds the hot records and grid lines of fewer scenes; a
+// per-scene launch takes the actors perm[seg[0], seg[1]) of its scene; single-scene
+// launches take rays in claim order (ray_perm).  Outputs stay actor-major.  The traced
+// values do not depend on the order.
 template <bool kFan, bool kMulti>
 __device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w, uint32_t seg_base)
 {
