@@ -771,3 +771,75 @@ def test_scene_tables_per_scene_launches_and_multi_scene_kernel(n_scenes):
     bad = np.nonzero((scene < 0) | (scene >= n_scenes))[0]
     assert bad.size == 4
     assert np.all(np.isnan(got[0][bad])) and np.all(got[1][bad] == 0) and np.all(got[2][bad] == 0)
+
+
+def test_concurrent_callers_on_their_own_streams():
+    """The reference's trainer casts from several rollout groups at once, each on its own
+    torch stream (the C ABI is reentrant: ctypes drops the GIL during the call).  Four
+    host threads, each on its own stream with its own poses and outputs, alternate
+    single-scene casts (claim order in the call's workspace) and three-scene casts
+    (per-scene launches on the library's shared streams, forked from and joined back to
+    the caller's stream).  Every result equals the same cast made alone."""
+    import threading
+
+    cfg1, cfg3 = scenes.CONFIGS[1], scenes.CONFIGS[3]
+    cs = workloads.compiled_scene(1)
+    multi = [workloads.compiled_scene(3, s, resolution=64) for s in range(3)]
+    single = tracer.SceneSet([tracer.NodePool.from_words(cs.words, dev())], [cs.bbox_min], [cs.bbox_max],
+                             [cs.hit_epsilon])
+    table = tracer.SceneSet([tracer.NodePool.from_words(c.words, dev()) for c in multi], [c.bbox_min for c in multi],
+                            [c.bbox_max for c in multi], [c.hit_epsilon for c in multi])
+    fan1 = torch.from_numpy(workloads.fan_for(1)).to(dev())
+    fan3 = torch.from_numpy(workloads.fan_for(3)).to(dev())
+
+    def job(i):
+        pb1 = workloads.poses_for(1, [cs], actors=16, seed_offset=100 + i)
+        pb3 = workloads.poses_for(3, multi, actors=48, seed_offset=200 + i)
+        p1 = tracer.make_poses(torch.from_numpy(pb1.position).to(dev()), torch.from_numpy(pb1.yaw).to(dev()),
+                               torch.from_numpy(pb1.pitch).to(dev()))
+        p3 = tracer.make_poses(torch.from_numpy(pb3.position).to(dev()), torch.from_numpy(pb3.yaw).to(dev()),
+                               None, torch.from_numpy(pb3.scene).to(dev()))
+        return [(single, p1, fan1, cfg1, True), (table, p3, fan3, cfg3, False)]
+
+    def cast(sset, p, fan, cfg, pitch):
+        n = p.shape[0] * fan.shape[0]
+        d = torch.empty(n, device=dev())
+        s = torch.empty(n, dtype=torch.int32, device=dev())
+        k = torch.empty(n, dtype=torch.int32, device=dev())
+        tracer.cast_fan(sset, p, fan, d, s, max_steps=cfg.max_steps, max_distance=cfg.max_distance, use_pitch=pitch,
+                        out_steps=k)
+        return d, s, k
+
+    jobs = [job(i) for i in range(4)]
+    torch.cuda.synchronize()
+    want = [[tuple(x.cpu() for x in cast(*c)) for c in js] for js in jobs]
+    got = [[None, None] for _ in jobs]
+    errors = []
+
+    def worker(i):
+        try:
+            st = torch.cuda.Stream(dev())
+            st.wait_stream(torch.cuda.current_stream(dev()))
+            with torch.cuda.stream(st):
+                for rep in range(6):
+                    c = jobs[i][rep % 2]
+                    out = cast(*c)
+                    got[i][rep % 2] = out
+                st.synchronize()
+        except Exception as exc:  # reported below; a thread's failure must fail the test
+            errors.append(repr(exc))
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    torch.cuda.synchronize()
+    for i in range(4):
+        for j in range(2):
+            gd, gs, gk = (x.cpu() for x in got[i][j])
+            wd, ws, wk = want[i][j]
+            assert_bits_equal(gd.numpy(), wd.numpy(), f"thread {i} cast {j} dist")
+            assert_equal(gs.numpy(), ws.numpy(), f"thread {i} cast {j} sem")
+            assert_equal(gk.numpy(), wk.numpy(), f"thread {i} cast {j} steps")
