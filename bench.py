@@ -492,9 +492,10 @@ def run_navi(args) -> None:
                 "descent": args.descent,
             },
             # per step: one scene: the claim-order key and scatter kernels and the trace kernel;
-            # 2-64 scenes: the scene sort, one trace launch per scene and the unknown-scene fill
+            # 2-64 scenes: the scene sort, per scene the key, scatter and trace kernels, and
+            # the unknown-scene fill
             "gpu_launches": args.steps * (3 if len(scene_list) == 1 else
-                                          (len(scene_list) + 2 if len(scene_list) <= 64 else 2)),
+                                          (3 * len(scene_list) + 2 if len(scene_list) <= 64 else 2)),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "e2e_fan": e2e_fan,

@@ -138,9 +138,11 @@ TSDF_API int tsdf_scenes_destroy(tsdf_scenes* scenes);
 
 /* Device bytes of workspace tsdf_cast_fan needs for n_actors x rays_per_actor rays
  * on `scenes`: the work counter and, for a table of one scene, the claim order (as
- * tsdf_workspace_bytes), for more than one scene the actor order by scene (4 bytes
- * per actor, rounded up to 16) and 1 KB of per-scene bounds and counters.
- * scenes = NULL gives the larger of the two. */
+ * tsdf_workspace_bytes); for more than one scene the actor order by scene (4 bytes
+ * per actor, rounded up to 16) and 1 KB of per-scene bounds and counters, and for
+ * tables of up to 64 scenes (traced one launch per scene) each scene's claim order:
+ * 32 KB of bucket counts plus 5 bytes per ray (rounded up to 16).  scenes = NULL
+ * gives the largest of these. */
 TSDF_API uint64_t tsdf_fan_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors,
                                            int64_t rays_per_actor);
 

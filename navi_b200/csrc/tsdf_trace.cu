@@ -165,6 +165,10 @@ __device__ __forceinline__ uint32_t work_ray(const TraceArgs& a, uint32_t w, uin
 {
     if constexpr (kFan && !kMulti) {
         if (a.seg) {
+            if (a.ray_perm) {  // claim order of the scene's rays: a work item of the scene
+                w = __ldg(a.ray_perm + seg_base * a.rays_per_actor + w);
+                if (!checked(a.err, w < a.n_rays, kErrActor)) w = 0;
+            }
             const uint32_t slot = div_rpa(a, w);
             uint32_t actor = __ldg(a.perm + seg_base + slot);
             if (!checked(a.err, actor < a.n_rays / a.rays_per_actor, kErrActor)) actor = 0;
@@ -760,7 +764,45 @@ __device__ __forceinline__ uint32_t claim_ray(uint32_t& q_next, uint32_t& q_end,
 // long ones run while the short ones fill the GPU (config 2: 15% shorter launches).  The
 // key is only a schedule; every ray is traced exactly as before.  Rays go into
 // kOrderBuckets buckets of exit distance, counted, then scattered longest bucket first.
+// A per-scene launch of a scene table orders its own scene's rays the same way.
 constexpr int kOrderBuckets = 64;
+
+// Work items of a claim order: the launch's rays, or for a per-scene launch the rays of
+// its scene's actors perm[seg[0], seg[1]) (read on the device).  Keys and order entries
+// live at [base, base + n) of their arrays; an order entry is a work item w < n.
+struct OrderRange {
+    uint32_t n, base, seg_base;
+};
+
+template <bool kFan>
+__device__ __forceinline__ OrderRange order_range(const TraceArgs& a)
+{
+    OrderRange r{a.n_rays, 0u, 0u};
+    if constexpr (kFan) {
+        if (a.seg) {
+            const uint32_t n_actors = a.n_rays / a.rays_per_actor;
+            const uint32_t end = min(__ldg(a.seg + 1), n_actors);
+            r.seg_base = min(__ldg(a.seg), end);
+            r.n = (end - r.seg_base) * a.rays_per_actor;
+            r.base = r.seg_base * a.rays_per_actor;
+        }
+    }
+    return r;
+}
+
+// Ray of work item w < rg.n.
+template <bool kFan>
+__device__ __forceinline__ uint32_t order_ray(const TraceArgs& a, const OrderRange& rg, uint32_t w)
+{
+    if constexpr (kFan) {
+        if (a.seg) {
+            const uint32_t slot = div_rpa(a, w);
+            const uint32_t actor = __ldg(a.perm + rg.seg_base + slot);
+            return actor * a.rays_per_actor + (w - slot * a.rays_per_actor);
+        }
+    }
+    return w;
+}
 
 template <bool kFan>
 __global__ void __launch_bounds__(256) order_key_kernel(const TraceArgs a, float buckets_per_unit,
@@ -769,12 +811,13 @@ __global__ void __launch_bounds__(256) order_key_kernel(const TraceArgs a, float
     __shared__ unsigned int h[kOrderBuckets];
     for (int i = threadIdx.x; i < kOrderBuckets; i += blockDim.x) h[i] = 0;
     __syncthreads();
+    const OrderRange rg = order_range<kFan>(a);
     const float3 lo = make_float3(a.scene.bmin[0], a.scene.bmin[1], a.scene.bmin[2]);
     const float3 hi = make_float3(a.scene.bmax[0], a.scene.bmax[1], a.scene.bmax[2]);
-    for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < a.n_rays; r += gridDim.x * blockDim.x) {
+    for (uint32_t w = blockIdx.x * blockDim.x + threadIdx.x; w < rg.n; w += gridDim.x * blockDim.x) {
         float3 o, d;
         int scene = 0;
-        load_ray<kFan>(a, r, o, d, scene);
+        load_ray<kFan>(a, order_ray<kFan>(a, rg, w), o, d, scene);
         const float inf = __int_as_float(0x7f800000);
         const float tx = d.x > 0.f ? (hi.x - o.x) / d.x : (d.x < 0.f ? (lo.x - o.x) / d.x : inf);
         const float ty = d.y > 0.f ? (hi.y - o.y) / d.y : (d.y < 0.f ? (lo.y - o.y) / d.y : inf);
@@ -782,7 +825,7 @@ __global__ void __launch_bounds__(256) order_key_kernel(const TraceArgs a, float
         const float te = fminf(fminf(tx, ty), tz) * buckets_per_unit;
         const int b = (te >= 0.f) ? min(kOrderBuckets - 1, static_cast<int>(fminf(te, 1.0e9f))) : 0;
         const unsigned int k = static_cast<unsigned int>(kOrderBuckets - 1 - b);  // longest first
-        key[r] = static_cast<uint8_t>(k);
+        key[rg.base + w] = static_cast<uint8_t>(k);
         atomicAdd(&h[k], 1u);
     }
     __syncthreads();
@@ -790,19 +833,19 @@ __global__ void __launch_bounds__(256) order_key_kernel(const TraceArgs a, float
         if (h[i]) atomicAdd(&hist[i], h[i]);
 }
 
-// One tile of kOrderTile rays per block: ranks within the tile from shared-memory counters,
-// then one global reservation per bucket and block (a global atomic per ray would
-// serialise on the few buckets that hold most rays).
+// Tiles of kOrderTile work items, looped over by a persistent grid: ranks within the tile
+// from shared-memory counters, then one global reservation per bucket and tile (a global
+// atomic per ray would serialise on the few buckets that hold most rays).
 constexpr int kOrderPerThread = 8;
 constexpr int kOrderTile = 256 * kOrderPerThread;
 
-__global__ void __launch_bounds__(256) order_scatter_kernel(const uint8_t* __restrict__ key, uint32_t n,
+template <bool kFan>
+__global__ void __launch_bounds__(256) order_scatter_kernel(const TraceArgs a, const uint8_t* __restrict__ key,
                                                             const unsigned int* __restrict__ hist,
                                                             unsigned int* __restrict__ cursor, uint32_t* __restrict__ perm)
 {
     __shared__ unsigned int off[kOrderBuckets];
     __shared__ unsigned int cnt[kOrderBuckets];
-    if (threadIdx.x < kOrderBuckets) cnt[threadIdx.x] = 0;
     if (threadIdx.x == 0) {
         unsigned int run = 0;
         for (int b = 0; b < kOrderBuckets; ++b) {
@@ -810,28 +853,33 @@ __global__ void __launch_bounds__(256) order_scatter_kernel(const uint8_t* __res
             run += hist[b];
         }
     }
-    __syncthreads();
-    const uint32_t tile = blockIdx.x * static_cast<uint32_t>(kOrderTile);
-    uint8_t bk[kOrderPerThread];
-    unsigned int rank[kOrderPerThread];
+    const OrderRange rg = order_range<kFan>(a);
+    for (uint32_t tile = blockIdx.x * static_cast<uint32_t>(kOrderTile); tile < rg.n;
+         tile += gridDim.x * static_cast<uint32_t>(kOrderTile)) {
+        if (threadIdx.x < kOrderBuckets) cnt[threadIdx.x] = 0;
+        __syncthreads();
+        uint8_t bk[kOrderPerThread];
+        unsigned int rank[kOrderPerThread];
 #pragma unroll
-    for (int i = 0; i < kOrderPerThread; ++i) {
-        const uint32_t r = tile + i * 256u + threadIdx.x;
-        if (r < n) {
-            bk[i] = key[r];
-            rank[i] = atomicAdd(&cnt[bk[i]], 1u);
+        for (int i = 0; i < kOrderPerThread; ++i) {
+            const uint32_t w = tile + i * 256u + threadIdx.x;
+            if (w < rg.n) {
+                bk[i] = key[rg.base + w];
+                rank[i] = atomicAdd(&cnt[bk[i]], 1u);
+            }
         }
-    }
-    __syncthreads();
-    if (threadIdx.x < kOrderBuckets) {
-        const unsigned int c = cnt[threadIdx.x];
-        cnt[threadIdx.x] = c ? off[threadIdx.x] + atomicAdd(&cursor[threadIdx.x], c) : 0u;
-    }
-    __syncthreads();
+        __syncthreads();
+        if (threadIdx.x < kOrderBuckets) {
+            const unsigned int c = cnt[threadIdx.x];
+            cnt[threadIdx.x] = c ? off[threadIdx.x] + atomicAdd(&cursor[threadIdx.x], c) : 0u;
+        }
+        __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kOrderPerThread; ++i) {
-        const uint32_t r = tile + i * 256u + threadIdx.x;
-        if (r < n) perm[cnt[bk[i]] + rank[i]] = r;
+        for (int i = 0; i < kOrderPerThread; ++i) {
+            const uint32_t w = tile + i * 256u + threadIdx.x;
+            if (w < rg.n) perm[rg.base + cnt[bk[i]] + rank[i]] = w;
+        }
+        __syncthreads();  // cnt is reset for the next tile
     }
 }
 
@@ -1200,6 +1248,17 @@ uint64_t order_scratch_bytes(int64_t n_rays)
 }
 constexpr int64_t kSmemReservedPerBlock = 1024;  // shared memory the driver reserves per resident block
 
+// Buckets of the claim order per unit of exit distance: kOrderBuckets over the box diagonal.
+float exit_buckets_per_unit(const TsdfSceneDev& s)
+{
+    double diag2 = 0.0;
+    for (int i = 0; i < 3; ++i) {
+        const double ext = static_cast<double>(s.bmax[i]) - s.bmin[i];
+        diag2 += ext * ext;
+    }
+    return static_cast<float>(kOrderBuckets / std::sqrt(diag2));
+}
+
 template <bool kFan, bool kMulti>
 int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream, bool order = true,
            unsigned int* counter = nullptr)
@@ -1261,26 +1320,22 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     }
     if constexpr (!kMulti) {
         // claim order into the workspace after the counter: bucket counts and cursors,
-        // the order itself, the per-ray bucket keys
-        a.ray_perm = nullptr;
+        // the order itself, the per-ray bucket keys (per-scene launches bring their own)
+        if (order) a.ray_perm = nullptr;
         if (order && g_order.load() == 1) {
             const size_t n = a.n_rays;
             auto* hist = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + kScratchOffset);
             unsigned int* cursor = hist + kOrderBuckets;
             auto* perm = reinterpret_cast<uint32_t*>(cursor + kOrderBuckets);
             auto* key = reinterpret_cast<uint8_t*>(perm + n);
-            double diag2 = 0.0;
-            for (int i = 0; i < 3; ++i) {
-                const double ext = static_cast<double>(a.scene.bmax[i]) - a.scene.bmin[i];
-                diag2 += ext * ext;
-            }
-            const float buckets_per_unit = static_cast<float>(kOrderBuckets / std::sqrt(diag2));
+            const float buckets_per_unit = exit_buckets_per_unit(a.scene);
             const unsigned kb = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sms) * 8));
             e = cudaMemsetAsync(hist, 0, 2 * kOrderBuckets * sizeof(unsigned int), stream);
             if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(claim order)");
             order_key_kernel<kFan><<<kb, 256, 0, stream>>>(a, buckets_per_unit, key, hist);
-            order_scatter_kernel<<<static_cast<unsigned>((n + kOrderTile - 1) / kOrderTile), 256, 0, stream>>>(
-                key, a.n_rays, hist, cursor, perm);
+            order_scatter_kernel<kFan><<<static_cast<unsigned>(std::min<int64_t>((n + kOrderTile - 1) / kOrderTile,
+                                                                                 static_cast<int64_t>(sms) * 8)),
+                                         256, 0, stream>>>(a, key, hist, cursor, perm);
             e = cudaGetLastError();
             if (e != cudaSuccess) return cuda_fail(e, "claim-order launch");
             a.ray_perm = perm;
@@ -1372,6 +1427,9 @@ uint32_t clamp_chunk()
 constexpr int kMaxPerSceneLaunch = 64;
 constexpr size_t kPerSceneBytes = 1024;  // (kMaxPerSceneLaunch + 2) bounds + 2 words per launch
 static_assert((kMaxPerSceneLaunch + 2) * 4 + kMaxPerSceneLaunch * 8 <= kPerSceneBytes, "per-scene workspace");
+// claim order of each scene's rays: bucket counts and cursors per scene, then the order
+// and the keys of all rays (each scene's at its own rays' offset)
+constexpr size_t kPerSceneOrderBytes = static_cast<size_t>(kMaxPerSceneLaunch) * 2 * kOrderBuckets * 4;
 std::atomic<int64_t> g_per_scene{1};
 
 size_t actor_order_bytes(int64_t n_actors)
@@ -1424,10 +1482,19 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
     char* ws = static_cast<char*>(workspace);
     auto* seg = reinterpret_cast<uint32_t*>(ws + kScratchOffset + actor_order_bytes(n_actors));
     auto* counters = seg + (kMaxPerSceneLaunch + 2);
+    auto* hist = reinterpret_cast<unsigned int*>(ws + kScratchOffset + actor_order_bytes(n_actors) + kPerSceneBytes);
+    auto* ray_order = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(hist) + kPerSceneOrderBytes);
+    auto* keys = reinterpret_cast<uint8_t*>(ray_order + a.n_rays);
+    const bool order = g_order.load() == 1;
     int rc = sort_by_scene(a, scenes, n_actors, ws + kScratchOffset, stream, seg);
     if (rc != TSDF_OK) return rc;
     cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned int) * scenes->n, stream);
+    if (e == cudaSuccess && order)
+        e = cudaMemsetAsync(hist, 0, 2 * kOrderBuckets * sizeof(unsigned int) * scenes->n, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(per-scene counters)");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scenes->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     const bool grid_ok = g_descent.load() == 0;
     SceneStreams* st = scene_streams(scenes->device);
     std::unique_lock<std::mutex> hold;
@@ -1447,8 +1514,19 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
                                                            static_cast<int64_t>(b.scene.n_recs)));
         const bool grid = grid_ok && b.scene.depth >= 0;
         if (!grid) b.scene.depth = -1;
-        rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, b, scenes->device, workspace,
-                                 st ? st->s[s % kPerSceneStreams] : stream, /*order=*/false, counters + 2 * s);
+        const cudaStream_t ss = st ? st->s[s % kPerSceneStreams] : stream;
+        b.ray_perm = nullptr;
+        if (order) {  // the scene's rays by box-exit distance, longest first
+            unsigned int* h = hist + 2 * kOrderBuckets * s;
+            const unsigned grid_n = static_cast<unsigned>(sms) * 8u;
+            order_key_kernel<true><<<grid_n, 256, 0, ss>>>(b, exit_buckets_per_unit(b.scene), keys, h);
+            order_scatter_kernel<true><<<grid_n, 256, 0, ss>>>(b, keys, h, h + kOrderBuckets, ray_order);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return cuda_fail(e, "per-scene claim-order launch");
+            b.ray_perm = ray_order;
+        }
+        rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, b, scenes->device, workspace, ss,
+                                 /*order=*/false, counters + 2 * s);
         if (rc != TSDF_OK) return rc;
     }
     if (st) {
@@ -1458,9 +1536,6 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
         }
         if (e != cudaSuccess) return cuda_fail(e, "joining the per-scene streams");
     }
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scenes->device);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     unknown_scene_kernel<<<static_cast<unsigned>(sms), 256, 0, stream>>>(
         seg + scenes->n, a.perm, static_cast<uint32_t>(n_actors), a.rays_per_actor, a.out_d, a.out_s, a.out_steps);
     e = cudaGetLastError();
@@ -1580,7 +1655,10 @@ uint64_t tsdf_workspace_bytes(int64_t n_rays)
 uint64_t tsdf_fan_workspace_bytes(const tsdf_scenes* scenes, int64_t n_actors, int64_t rays_per_actor)
 {
     if (n_actors <= 0 || rays_per_actor <= 0) return kScratchOffset;
-    const uint64_t by_scene = actor_order_bytes(n_actors) + kPerSceneBytes;
+    const uint64_t n_rays = static_cast<uint64_t>(n_actors) * static_cast<uint64_t>(rays_per_actor);
+    const uint64_t by_scene = actor_order_bytes(n_actors) + kPerSceneBytes +
+                              ((!scenes || scenes->n <= kMaxPerSceneLaunch)
+                                   ? kPerSceneOrderBytes + 4u * n_rays + ((n_rays + 15u) & ~uint64_t(15)) : 0u);
     const uint64_t order = order_scratch_bytes(n_actors * rays_per_actor);
     if (!scenes) return kScratchOffset + std::max(by_scene, order);
     return kScratchOffset + (scenes->n > 1 ? by_scene : order);

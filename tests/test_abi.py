@@ -41,8 +41,11 @@ def test_version_and_workspace_query():
     # counter block + 128 bucket words + 4-byte order + 1-byte key per ray, rounded to 16
     assert lib.tsdf_workspace_bytes(1000) == 256 + 512 + 4000 + 1008
     assert lib.tsdf_fan_workspace_bytes(None, 10, 0) == 256
-    assert lib.tsdf_fan_workspace_bytes(None, 10, 100) == 256 + 512 + 4000 + 1008
-    assert lib.tsdf_fan_workspace_bytes(None, 4096, 1) == 256 + 512 + 5 * 4096
+    # scenes = NULL: the larger of one scene's claim order and a scene table's (actor order
+    # rounded to 16, 1 KB of ranges and counters, 32 KB of per-scene bucket counts, the
+    # 4-byte order and 1-byte key of every ray)
+    assert lib.tsdf_fan_workspace_bytes(None, 10, 100) == 256 + 48 + 1024 + 32768 + 4000 + 1008
+    assert lib.tsdf_fan_workspace_bytes(None, 4096, 1) == 256 + 16384 + 1024 + 32768 + 4 * 4096 + 4096
     assert lib.tsdf_observe_workspace_bytes(None, 10, 100) == lib.tsdf_fan_workspace_bytes(None, 10, 100)
 
 
