@@ -54,8 +54,10 @@ def test_option_knobs_validate_their_range():
     old = ctypes.c_int64()
     assert lib.tsdf_set_option(b"chunk", 64, ctypes.byref(old)) == 0
     assert lib.tsdf_set_option(b"chunk", old.value, None) == 0
-    assert lib.tsdf_set_option(b"chunk", 0, None) != 0
+    assert lib.tsdf_set_option(b"chunk", -1, None) != 0
     assert b"chunk" in lib.tsdf_last_error()
+    assert lib.tsdf_set_option(b"chunk", 1025, None) != 0
+    assert old.value == 0  # the default: chosen per launch
     assert lib.tsdf_set_option(b"order", 2, None) != 0
     assert b"order" in lib.tsdf_last_error()
     assert lib.tsdf_set_option(b"per_scene", 2, None) != 0
