@@ -408,7 +408,15 @@ def cast_fan(
     use_pitch: bool = False,
     out_steps: torch.Tensor | None = None,
 ) -> None:
-    """Trace every actor's fan: out[a, r] for pose a and local direction fan_dirs[r]."""
+    """Trace every actor's fan: out[a, r] for pose a and local direction fan_dirs[r].
+
+    Each actor is traced in the scene its pose names (``make_poses(..., scene=)``); an
+    index outside the table gives NaN distance, semantic 0 and 0 steps.  A table of one
+    scene is one launch with rays claimed longest-first; a table of 2 to 64 scenes is one
+    launch per scene, on library streams forked from and joined back to the current
+    stream, so the outputs are ready for anything later on the current stream.  The
+    workspace (``tsdf_fan_workspace_bytes``) is allocated here on the current stream.
+    """
     if poses.dtype != torch.float32 or poses.dim() != 2 or poses.shape[1] != 8 or not poses.is_contiguous():
         raise RuntimeError("poses must be a contiguous float32 [actors, 8] tensor (see make_poses)")
     if fan_dirs.dtype != torch.float32 or fan_dirs.dim() != 2 or fan_dirs.shape[1] != 3 or not fan_dirs.is_contiguous():
