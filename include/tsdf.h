@@ -198,9 +198,11 @@ TSDF_API int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* p
  * a 256-byte static device array inside the library, held by every GPU that
  * loads it; its address is looked up by the first call on each device, which
  * must come before any stream capture.  All calls share that array: calls whose
- * kernels may overlap on the GPU race and must be ordered on one stream.
+ * kernels may overlap on the GPU race and must be ordered on one stream.  The
+ * looked-up address is tied to the device's context: after cudaDeviceReset of
+ * that device it is stale, and the entry point must not be called on it again.
  * Allocates nothing: no cudaMalloc, no cudaFree.  With no room for a claim order,
- * rays are claimed in index order. */
+ * rays are claimed in index order.  Leaves the caller's current device as it was. */
 TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, const float* dirs,
                                int64_t n_rays, float* out_dist, int32_t* out_sem, int32_t* out_steps,
                                int max_steps, float max_distance, const float bbox_min[3],

@@ -10,6 +10,7 @@
                      that its float arithmetic matches the reference compiler's)
 - libnavi_gmdag_gpu.so : the device scene compiler (nvcc sm_100a, -fmad=false,
                      IEEE division / sqrt; same words as libnavi_gmdag.so)
+- libnavi_probe.so : the L2 read-bandwidth probe of the benchmark's roofline
 
 Both are rebuilt only when a source is newer than the library.
 """
@@ -119,8 +120,22 @@ def build_gmdag_gpu(force: bool = False) -> Path:
     return out
 
 
+def build_probe(force: bool = False) -> Path:
+    """libnavi_probe.so: the L2 read-bandwidth probe bench.py reports the L2 roofline against."""
+    out = LIB / "libnavi_probe.so"
+    src = CSRC / "peak_probe.cu"
+    if force or _stale(out, [src]):
+        LIB.mkdir(parents=True, exist_ok=True)
+        tmp = out.with_suffix(".so.tmp")
+        _run([_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", str(src),
+              "-o", str(tmp)])
+        tmp.replace(out)
+    return out
+
+
 def build_all(force: bool = False) -> list[Path]:
-    return [build_tsdf(force), build_tsdf(force, bounds_check=True), build_gmdag(force), build_gmdag_gpu(force)]
+    return [build_tsdf(force), build_tsdf(force, bounds_check=True), build_gmdag(force), build_gmdag_gpu(force),
+            build_probe(force)]
 
 
 if __name__ == "__main__":

@@ -458,6 +458,24 @@ T read_back(const T* dev, cudaStream_t st)
 
 // ------------------------------------------------------------------ host driver
 
+// Puts the caller's current device back when an entry point returns (the compiler
+// makes its own device current while it runs); declared before the compiler, so it
+// is destroyed after the compiler's buffers are freed.
+struct KeepCurrentDevice {
+    int prev = -1;
+    KeepCurrentDevice()
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            cudaGetLastError();
+            prev = -1;
+        }
+    }
+    ~KeepCurrentDevice()
+    {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
 class DeviceCompiler {
 public:
     DeviceCompiler(int N, int device) : N_(N), device_(device)
@@ -879,6 +897,7 @@ int gmdag_gpu_compile_mesh(const float* verts, uint64_t n_verts, const uint32_t*
         gmdag::mesh_bounds(verts, n_verts, resolution, r->bmin, r->bmax, &r->voxel);
         const gmdag::GridFrame f = gmdag::grid_frame(r->bmin, r->bmax, N);
         auto t0 = Clock::now();
+        KeepCurrentDevice keep;
         DeviceCompiler dc(N, device);
         dc.alloc_grid();
         r->timing.upload_ms = ms_since(t0);
@@ -906,6 +925,7 @@ int gmdag_gpu_compute_sdf(const float* verts, uint64_t n_verts, const uint32_t* 
         const int N = static_cast<int>(resolution);
         gmdag::mesh_bounds(verts, n_verts, resolution, bmin, bmax, voxel);
         const gmdag::GridFrame f = gmdag::grid_frame(bmin, bmax, N);
+        KeepCurrentDevice keep;
         DeviceCompiler dc(N, device);
         dc.alloc_grid();
         dc.seed(verts, n_verts, idx, n_tri, bmin, f);
@@ -927,6 +947,7 @@ int gmdag_gpu_compile_grid(const float* grid, uint32_t resolution, float voxel, 
         r->voxel = voxel;
         for (int a = 0; a < 3; ++a) r->bmax[a] = voxel * static_cast<float>(N);
         auto t0 = Clock::now();
+        KeepCurrentDevice keep;
         DeviceCompiler dc(N, device);
         dc.upload_grid(grid);
         r->timing.upload_ms = ms_since(t0);

@@ -116,4 +116,35 @@ inline void set_grid_scale(TsdfSceneDev& d)
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
+
+// Makes `device` the calling thread's current device for the scope and puts the
+// caller's current device back when the scope ends, so that a call on a pool of
+// another GPU does not move the caller's later allocations and launches (torch keeps
+// its current device in the same per-thread runtime state).
+class DeviceScope {
+public:
+    explicit DeviceScope(int device)
+    {
+        if (cudaGetDevice(&prev_) != cudaSuccess) {
+            cudaGetLastError();
+            prev_ = -1;
+        }
+        if (prev_ != device) {
+            err_ = cudaSetDevice(device);
+            switched_ = err_ == cudaSuccess && prev_ >= 0;
+        }
+    }
+    ~DeviceScope()
+    {
+        if (switched_) cudaSetDevice(prev_);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+    cudaError_t error() const { return err_; }
+
+private:
+    int prev_ = -1;
+    bool switched_ = false;
+    cudaError_t err_ = cudaSuccess;
+};
 }  // namespace tsdf

@@ -288,7 +288,8 @@ static int check_device(int device)
 // Device copy of a host pool (records + out-of-line leaves).
 static int upload_pool(const tsdf::HostPool& hp, uint64_t source_words, int device, tsdf_pool** out_pool)
 {
-    cudaError_t e = cudaSetDevice(device);
+    tsdf::DeviceScope scope(device);
+    cudaError_t e = scope.error();
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     auto* pool = new (std::nothrow) tsdf_pool();
     if (!pool) return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
@@ -362,12 +363,15 @@ int tsdf_pool_create_from_device(const uint64_t* device_words, uint64_t n_words,
     } catch (const std::bad_alloc&) {
         return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
     }
-    cudaError_t e = cudaSetDevice(device);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    e = cudaMemcpyAsync(host.data(), device_words, n_words * sizeof(uint64_t),
-                        cudaMemcpyDeviceToHost, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaError_t e;
+    {
+        tsdf::DeviceScope scope(device);
+        e = scope.error();
+        if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        e = cudaMemcpyAsync(host.data(), device_words, n_words * sizeof(uint64_t), cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "copying the DAG words to the host");
     return tsdf_pool_create(host.data(), n_words, device, flags, out_pool);
 }
@@ -434,14 +438,15 @@ int tsdf_pool_save(const tsdf_pool* pool, const char* path)
     } catch (const std::bad_alloc&) {
         return fail(TSDF_ERR_NO_MEMORY, "out of host memory");
     }
-    int prev = 0;
-    cudaGetDevice(&prev);
-    cudaError_t e = cudaSetDevice(pool->device);
-    if (e == cudaSuccess && !recs.empty())
-        e = cudaMemcpy(recs.data(), pool->d_recs, recs.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess && !ext.empty())
-        e = cudaMemcpy(ext.data(), pool->d_ext, ext.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost);
-    cudaSetDevice(prev);
+    cudaError_t e;
+    {
+        tsdf::DeviceScope scope(pool->device);
+        e = scope.error();
+        if (e == cudaSuccess && !recs.empty())
+            e = cudaMemcpy(recs.data(), pool->d_recs, recs.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && !ext.empty())
+            e = cudaMemcpy(ext.data(), pool->d_ext, ext.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "copying the node pool to the host");
     PoolFileHeader h{};
     std::memcpy(h.magic, "NPOL", 4);
@@ -502,12 +507,12 @@ int tsdf_pool_load(const char* path, int device, tsdf_pool** out_pool)
 int tsdf_pool_destroy(tsdf_pool* pool)
 {
     if (!pool) return TSDF_OK;
-    int prev = 0;
-    cudaGetDevice(&prev);
-    cudaSetDevice(pool->device);
-    cudaError_t e1 = cudaFree(pool->d_recs);
-    cudaError_t e2 = cudaFree(pool->d_ext);
-    cudaSetDevice(prev);
+    cudaError_t e1, e2;
+    {
+        tsdf::DeviceScope scope(pool->device);
+        e1 = cudaFree(pool->d_recs);
+        e2 = cudaFree(pool->d_ext);
+    }
     delete pool;
     if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFree");
     if (e2 != cudaSuccess) return cuda_fail(e2, "cudaFree");
@@ -580,7 +585,8 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
         grid = grid && d.depth >= 0;
     }
     sc->grid = grid;
-    cudaError_t e = cudaSetDevice(device);
+    tsdf::DeviceScope scope(device);
+    cudaError_t e = scope.error();
     if (e == cudaSuccess && !lines.empty()) e = cudaMalloc(&sc->d_lines, lines.size() * sizeof(float));
     if (e == cudaSuccess && !lines.empty())
         e = cudaMemcpy(sc->d_lines, lines.data(), lines.size() * sizeof(float), cudaMemcpyHostToDevice);
@@ -604,12 +610,12 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
 int tsdf_scenes_destroy(tsdf_scenes* scenes)
 {
     if (!scenes) return TSDF_OK;
-    int prev = 0;
-    cudaGetDevice(&prev);
-    cudaSetDevice(scenes->device);
-    cudaError_t e = cudaFree(scenes->d_table);
-    cudaFree(scenes->d_lines);
-    cudaSetDevice(prev);
+    cudaError_t e;
+    {
+        tsdf::DeviceScope scope(scenes->device);
+        e = cudaFree(scenes->d_table);
+        cudaFree(scenes->d_lines);
+    }
     delete scenes;
     if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
     return TSDF_OK;

@@ -1236,9 +1236,10 @@ int common_checks(int64_t n_rays, float* out_d, int32_t* out_s, int max_steps, f
 
 enum class Kind { kFloat, kGrid };
 
-// Workspace layout: the work counter and error word, then from kScratchOffset either the
-// multi-scene actor order (4 bytes per actor) or the single-scene claim order
-// (order_scratch_bytes).
+// Workspace layout: the work counter and error word (kLaunchWords words, cleared by every
+// launch), then from kScratchOffset either the multi-scene actor order (4 bytes per actor)
+// or the single-scene claim order (order_scratch_bytes).
+constexpr size_t kLaunchWords = 2;
 constexpr size_t kScratchOffset = 256;
 
 uint64_t order_scratch_bytes(int64_t n_rays)
@@ -1259,15 +1260,102 @@ float exit_buckets_per_unit(const TsdfSceneDev& s)
     return static_cast<float>(kOrderBuckets / std::sqrt(diag2));
 }
 
+// Per-device launch constants, read once per device and kernel instead of on every
+// cast: the SM count, shared memory per SM, the resident blocks per SM of a kernel at a
+// dynamic shared-memory size, and the largest dynamic shared memory a kernel has been
+// allowed (cudaFuncAttributeMaxDynamicSharedMemorySize, per device and kernel).
+constexpr int kMaxInfoDevices = 64;
+struct DeviceInfo {
+    int sms = 0;
+    int smem_per_sm = 0;
+};
+struct OccupancyEntry {
+    int device;
+    const void* kern;
+    size_t smem;
+    int blocks;
+};
+struct SmemAttrEntry {
+    int device;
+    const void* kern;
+    size_t smem;
+};
+std::mutex g_info_mu;
+DeviceInfo g_info[kMaxInfoDevices];
+std::vector<OccupancyEntry> g_occupancy;  // under g_info_mu
+std::vector<SmemAttrEntry> g_smem_attr;   // under g_info_mu
+
+int device_info(int device, DeviceInfo& out)
+{
+    if (device < 0 || device >= kMaxInfoDevices) return fail(TSDF_ERR_INVALID, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_info_mu);
+    DeviceInfo& d = g_info[device];
+    if (d.sms == 0) {
+        int sms = 0, smem = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        d.smem_per_sm = smem;
+        d.sms = sms;
+    }
+    out = d;
+    return TSDF_OK;
+}
+
+// Lets `kern` launch with `smem` bytes of dynamic shared memory on the current device
+// (`device`), once per device, kernel and size above what was already allowed.
+int allow_smem(int device, const void* kern, size_t smem)
+{
+    if (smem <= 48u * 1024u) return TSDF_OK;
+    std::lock_guard<std::mutex> lock(g_info_mu);
+    for (SmemAttrEntry& en : g_smem_attr) {
+        if (en.device == device && en.kern == kern) {
+            if (en.smem >= smem) return TSDF_OK;
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+            en.smem = smem;
+            return TSDF_OK;
+        }
+    }
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    g_smem_attr.push_back({device, kern, smem});
+    return TSDF_OK;
+}
+
+// Resident blocks of kThreads threads per SM for `kern` at `smem` bytes (current device `device`).
+int resident_blocks(int device, const void* kern, size_t smem, int& blocks)
+{
+    {
+        std::lock_guard<std::mutex> lock(g_info_mu);
+        for (const OccupancyEntry& en : g_occupancy)
+            if (en.device == device && en.kern == kern && en.smem == smem) {
+                blocks = en.blocks;
+                return TSDF_OK;
+            }
+    }
+    int rc = allow_smem(device, kern, smem);
+    if (rc != TSDF_OK) return rc;
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    std::lock_guard<std::mutex> lock(g_info_mu);
+    g_occupancy.push_back({device, kern, smem, n});
+    blocks = n;
+    return TSDF_OK;
+}
+
 template <bool kFan, bool kMulti>
 int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t stream, bool order = true,
            unsigned int* counter = nullptr)
 {
-    cudaError_t e = cudaSetDevice(device);
+    tsdf::DeviceScope scope(device);
+    cudaError_t e = scope.error();
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    DeviceInfo info;
+    int rc = device_info(device, info);
+    if (rc != TSDF_OK) return rc;
+    const int sms = info.sms;
     void (*kern)(TraceArgs);
     size_t base;  // shared memory besides the staged records
     if (kind == Kind::kGrid) {
@@ -1280,31 +1368,24 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     }
     // Stage no more top records than the register-limited occupancy leaves room for:
     // a deep grid (2^11 lines per axis) with 1024 records would drop a block per SM.
+    const void* kid = reinterpret_cast<const void*>(kern);
     if (a.n_smem > 0) {
-        int sm_bytes = 0, reg_blocks = 0;
-        e = cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-        if (base > 48u * 1024u) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(base));
-            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-        }
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&reg_blocks, kern, kThreads, base);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        int reg_blocks = 0;
+        rc = resident_blocks(device, kid, base, reg_blocks);
+        if (rc != TSDF_OK) return rc;
         if (reg_blocks > 0) {
-            const int64_t per_block = static_cast<int64_t>(sm_bytes) / reg_blocks - kSmemReservedPerBlock;
+            const int64_t per_block = static_cast<int64_t>(info.smem_per_sm) / reg_blocks - kSmemReservedPerBlock;
             const int64_t fit = (per_block - static_cast<int64_t>(base)) / 32;
             a.n_smem = static_cast<uint32_t>(std::max<int64_t>(0, std::min<int64_t>(a.n_smem, fit)));
         }
     }
     const size_t smem = base + static_cast<size_t>(a.n_smem) * 32u;
-    if (smem > 48u * 1024u) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    }
+    rc = allow_smem(device, kid, smem);
+    if (rc != TSDF_OK) return rc;
     int per_sm = static_cast<int>(g_blocks_per_sm.load());
     if (per_sm <= 0) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        rc = resident_blocks(device, kid, smem, per_sm);
+        if (rc != TSDF_OK) return rc;
         if (per_sm <= 0) return fail(TSDF_ERR_INVALID, "trace kernel does not fit on an SM with this shared-memory stage");
     }
     const int64_t need = (static_cast<int64_t>(a.n_rays) + kThreads - 1) / kThreads;
@@ -1315,7 +1396,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     } else {
         a.counter = static_cast<unsigned int*>(workspace);
         a.err = a.counter + 1;
-        e = cudaMemsetAsync(workspace, 0, 2 * sizeof(unsigned int), stream);
+        e = cudaMemsetAsync(workspace, 0, kLaunchWords * sizeof(unsigned int), stream);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
     }
     if constexpr (!kMulti) {
@@ -1386,7 +1467,8 @@ int sort_by_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, voi
     a.n_scenes = static_cast<uint32_t>(scenes->n);
     a.perm = nullptr;
     if (static_cast<uint32_t>(scenes->n) > kMaxSortedScenes) return TSDF_OK;  // actor order as given
-    cudaError_t e = cudaSetDevice(scenes->device);
+    tsdf::DeviceScope scope(scenes->device);
+    cudaError_t e = scope.error();
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     auto* perm = static_cast<uint32_t*>(perm_mem);
     const size_t smem = (static_cast<size_t>(scenes->n) + 1) * sizeof(unsigned int);
@@ -1495,15 +1577,19 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
     auto* ray_order = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(hist) + kPerSceneOrderBytes);
     auto* keys = reinterpret_cast<uint8_t*>(ray_order + a.n_rays);
     const bool order = g_order.load() == 1;
-    int rc = sort_by_scene(a, scenes, n_actors, ws + kScratchOffset, stream, seg);
+    tsdf::DeviceScope scope(scenes->device);
+    cudaError_t e = scope.error();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    DeviceInfo info;
+    int rc = device_info(scenes->device, info);
     if (rc != TSDF_OK) return rc;
-    cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned int) * scenes->n, stream);
+    const int sms = info.sms;
+    rc = sort_by_scene(a, scenes, n_actors, ws + kScratchOffset, stream, seg);
+    if (rc != TSDF_OK) return rc;
+    e = cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned int) * scenes->n, stream);
     if (e == cudaSuccess && order)
         e = cudaMemsetAsync(hist, 0, 2 * kOrderBuckets * sizeof(unsigned int) * scenes->n, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(per-scene counters)");
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scenes->device);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     const bool grid_ok = g_descent.load() == 0;
     SceneStreams* st = scene_streams(scenes->device);
     std::unique_lock<std::mutex> hold;
@@ -1513,6 +1599,19 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
         for (int i = 0; i < kPerSceneStreams && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(st->s[i], st->fork, 0);
         if (e != cudaSuccess) return cuda_fail(e, "forking the per-scene streams");
     }
+    // After the fork every exit joins the side streams back to the caller's stream, the
+    // failing ones included, so that the caller's stream stays ordered after the work
+    // already queued there and a capture in progress sees no unjoined fork.
+    auto join = [&]() -> cudaError_t {
+        cudaError_t je = cudaSuccess;
+        if (!st) return je;
+        for (int i = 0; i < kPerSceneStreams; ++i) {
+            cudaError_t r = cudaEventRecord(st->join[i], st->s[i]);
+            if (r == cudaSuccess) r = cudaStreamWaitEvent(stream, st->join[i], 0);
+            if (je == cudaSuccess) je = r;
+        }
+        return je;
+    };
     for (int s = 0; s < scenes->n; ++s) {
         TraceArgs b = a;
         b.table = nullptr;
@@ -1532,20 +1631,21 @@ int trace_per_scene(TraceArgs& a, const tsdf_scenes* scenes, int64_t n_actors, v
             order_key_kernel<true><<<grid_n, 256, 0, ss>>>(b, exit_buckets_per_unit(b.scene), keys, h);
             order_scatter_kernel<true><<<grid_n, 256, 0, ss>>>(b, keys, h, h + kOrderBuckets, ray_order);
             e = cudaGetLastError();
-            if (e != cudaSuccess) return cuda_fail(e, "per-scene claim-order launch");
+            if (e != cudaSuccess) {
+                join();
+                return cuda_fail(e, "per-scene claim-order launch");
+            }
             b.ray_perm = ray_order;
         }
         rc = launch<true, false>(grid ? Kind::kGrid : Kind::kFloat, b, scenes->device, workspace, ss,
                                  /*order=*/false, counters + 2 * s);
-        if (rc != TSDF_OK) return rc;
-    }
-    if (st) {
-        for (int i = 0; i < kPerSceneStreams && e == cudaSuccess; ++i) {
-            e = cudaEventRecord(st->join[i], st->s[i]);
-            if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, st->join[i], 0);
+        if (rc != TSDF_OK) {
+            join();  // keeps the launch's error message: a join failure is secondary
+            return rc;
         }
-        if (e != cudaSuccess) return cuda_fail(e, "joining the per-scene streams");
     }
+    e = join();
+    if (e != cudaSuccess) return cuda_fail(e, "joining the per-scene streams");
     unknown_scene_kernel<<<static_cast<unsigned>(sms), 256, 0, stream>>>(
         seg + scenes->n, a.perm, static_cast<uint32_t>(n_actors), a.rays_per_actor, a.out_d, a.out_s, a.out_steps);
     e = cudaGetLastError();
@@ -1738,6 +1838,9 @@ int tsdf_cast_fan_observe(const tsdf_scenes* scenes, const tsdf_pose* poses, int
     ob.f_all = fa / static_cast<float>(n_rays);
     ob.f_fwd = fa / static_cast<float>(n_actors * 2 * static_cast<int64_t>(ob.fwd_half) * observe->elevation_bins);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    tsdf::DeviceScope scope(scenes->device);  // the observation pass launches on the scenes' device too
+    cudaError_t se = scope.error();
+    if (se != cudaSuccess) return cuda_fail(se, "cudaSetDevice");
     if (scenes->n == 1) {
         a.scene = scenes->host[0];
         a.n_smem = static_cast<uint32_t>(std::min<int64_t>(std::max<int64_t>(g_smem_records.load(), 0),
@@ -1821,7 +1924,10 @@ int tsdf_set_option(const char* key, int64_t value, int64_t* old_value)
 // device share the array and it keeps the last call's contents: the counter is
 // cleared (cudaMemsetAsync on the caller's stream) before every launch, and two
 // calls whose kernels overlap on the GPU (different streams, no ordering between
-// them) race on it and produce wrong outputs; order them on one stream.
+// them) race on it and produce wrong outputs; order them on one stream.  The
+// fetched address belongs to the device's current context: after cudaDeviceReset
+// on that device it is stale, so a process that resets a device must not call
+// this entry point on it again.
 // ============================================================================
 
 constexpr size_t kNoAllocScratchBytes = 256;  // stated maximum scratch of one cast
@@ -1861,8 +1967,8 @@ extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, co
                                  const float bbox_max[3], float hit_epsilon, void* stream)
 {
     if (!pool) return fail(TSDF_ERR_INVALID, "pool must not be null");
-    // the persistent kernel's only scratch is its work counter
-    const size_t need = sizeof(unsigned int);
+    // the persistent kernel's scratch: its work counter and the error word after it
+    const size_t need = kLaunchWords * sizeof(unsigned int);
     if (need > kNoAllocScratchBytes)
         return fail(TSDF_ERR_INVALID, "tsdf_cast_noalloc: the cast needs more scratch than the 256-byte static array");
     if (pool->device < 0 || pool->device >= kNoAllocMaxDevices)
@@ -1884,7 +1990,8 @@ extern "C" int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, co
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
         if (!g_noalloc_addr[pool->device]) {
-            cudaError_t e = cudaSetDevice(pool->device);
+            tsdf::DeviceScope scope(pool->device);  // the address is per device; the caller's device is kept
+            cudaError_t e = scope.error();
             if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
             void* addr = nullptr;
             e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);

@@ -26,7 +26,7 @@
  *   - a node index outside the payload is reported as an error instead of
  *     being read (the reference reads such words unchecked).
  *
- * Build: oracle/Makefile (gcc, -ffp-contract=off so that no other expression
+ * Build: oracle/build.py (gcc, -ffp-contract=off so that no other expression
  * is contracted; fmaf() is the C99 correctly rounded fused multiply-add).
  */
 #include <math.h>
