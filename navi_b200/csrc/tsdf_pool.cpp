@@ -573,12 +573,15 @@ int tsdf_scenes_create(const tsdf_pool* const* pools, int n, const float* bbox_m
         d.eps = hit_epsilon[i];
         d.depth = -1;
         if (p->height >= 0 && p->height <= tsdf::kMaxGridDepth) {
-            const size_t m = (size_t(1) << p->height) + 2;
-            line_off[i] = lines.size();
+            // rows of -inf, B[0..n], +inf (the kernels' line_row layout); `lines` points at B[0]
+            const size_t m = (size_t(1) << p->height) + 3;
+            line_off[i] = lines.size() + 1;
             lines.resize(lines.size() + 3 * m);
             bool ok = true;
-            for (int a = 0; a < 3; ++a)
+            for (int a = 0; a < 3; ++a) {
+                lines[line_off[i] + a * m - 1] = -std::numeric_limits<float>::infinity();
                 ok = ok && tsdf::build_grid_lines(d.bmin[a], d.bmax[a], p->height, &lines[line_off[i] + a * m]);
+            }
             if (ok) d.depth = p->height;
         }
         tsdf::set_grid_scale(d);

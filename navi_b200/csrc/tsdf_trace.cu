@@ -664,68 +664,71 @@ __device__ __forceinline__ bool cell_open(uint32_t c, int i, bool on)
     return static_cast<uint32_t>(i - cell_lo(c)) - o < (c >> 16) - o;
 }
 
+// Per-axis grid lines: rows of kLineRow(n) = n + 3 floats, -inf, B[0..n], +inf; `lines`
+// points at B[0] of axis 0, so line_at(axis, k) reads B[k] for k in [-1, n + 1].
+__host__ __device__ constexpr int line_row(int n) { return n + 3; }
+
 struct GridView {
-    const float* lines;  // [3][n + 1]
+    const float* lines;  // B[0] of axis 0; rows of line_row(n) floats
     int n;
 };
 
 template <bool kShared>
 __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
 {
-    const float* ptr = g.lines + axis * (g.n + 2) + k;
+    const float* ptr = g.lines + axis * line_row(g.n) + k;
     if constexpr (kShared) return *ptr;
     else return __ldg(ptr);
 }
 
-// index of the last grid line <= p (-1 below the box, n at or above its top face).
-// e = floor(u(p)) is within one cell of the answer (proved per table on the host,
-// build_grid_lines), so three neighbouring lines decide it without a loop.
+// Index of the last grid line <= p: -1 below the box, n at or above its top face (n + 1
+// for p = +inf, which every later test treats as outside), and whether p lies on it.
+// e = floor(u(p)), clamped to [0, n], is within one cell of the answer (proved per table
+// on the host, build_grid_lines), so three neighbouring lines decide it; the -inf / +inf
+// sentinels at both ends of the row make the box faces need no special case (NaN: -1).
 template <bool kShared>
-__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float b0, float bn,
-                                          float scale, bool& on)
+__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float b0, float scale, bool& on)
 {
-    const int e = max(min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n - 1), 1);
+    const int e = max(min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n), 0);
     const float lm = line_at<kShared>(g, axis, e - 1);
     const float l0 = line_at<kShared>(g, axis, e);
     const float lp = line_at<kShared>(g, axis, e + 1);
     const bool ge0 = p >= l0, gep = p >= lp;
-    int k = e - 1 + (ge0 ? 1 : 0) + (gep ? 1 : 0);
     on = p == (gep ? lp : (ge0 ? l0 : lm));
-    if (!(p >= b0)) {
-        on = false;
-        k = -1;
-    } else if (p >= bn) {
-        on = (p == bn);
-        k = g.n;
-    }
-    return k;
+    return e - 1 + (ge0 ? 1 : 0) + (gep ? 1 : 0);
 }
 
 // kernel.cu:54-85 with the void cell's faces read from the grid lines.  Approximate
-// quotients (within 2^-21 relative of the exact ones) pick the axes that can hold the
-// minimum; only those get the IEEE division, so the result is the reference's.
+// quotients (within 2^-21 relative of the exact ones) pick the axis of the minimum, which
+// alone gets the IEEE division: one division per lane, so a warp whose lanes leave their
+// cells through different faces runs one division sequence, not three.  Axes whose
+// approximate quotient lies within the approximation margin of the minimum (a near tie,
+// rare) get their IEEE division too, so the result is the reference's min over axes.
 template <bool kShared>
 __device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
                                                     uint32_t cx, uint32_t cy, uint32_t cz)
 {
     const float inf = __int_as_float(0x7f800000);
-    float ax = 0.f, ay = 0.f, az = 0.f, qx = inf, qy = inf, qz = inf;
-    if (d.x > kDirEps) ax = __fsub_rn(line_at<kShared>(g, 0, cell_hi(cx)), p.x);
-    else if (d.x < -kDirEps) ax = __fsub_rn(line_at<kShared>(g, 0, cell_lo(cx)), p.x);
-    if (d.y > kDirEps) ay = __fsub_rn(line_at<kShared>(g, 1, cell_hi(cy)), p.y);
-    else if (d.y < -kDirEps) ay = __fsub_rn(line_at<kShared>(g, 1, cell_lo(cy)), p.y);
-    if (d.z > kDirEps) az = __fsub_rn(line_at<kShared>(g, 2, cell_hi(cz)), p.z);
-    else if (d.z < -kDirEps) az = __fsub_rn(line_at<kShared>(g, 2, cell_lo(cz)), p.z);
     const bool vx = fabsf(d.x) > kDirEps, vy = fabsf(d.y) > kDirEps, vz = fabsf(d.z) > kDirEps;
-    if (vx) qx = __fdividef(ax, d.x);
-    if (vy) qy = __fdividef(ay, d.y);
-    if (vz) qz = __fdividef(az, d.z);
-    const float lim = __fmul_rn(fminf(fminf(qx, qy), qz), 1.0f + 0x1p-19f);
-    float t = kOutside;
-    if (vx && qx <= lim) t = fminf(t, __fdiv_rn(ax, d.x));
-    if (vy && qy <= lim) t = fminf(t, __fdiv_rn(ay, d.y));
-    if (vz && qz <= lim) t = fminf(t, __fdiv_rn(az, d.z));
-    return fmaxf(t, kVoidAdvance);
+    const float ax = __fsub_rn(line_at<kShared>(g, 0, d.x > 0.0f ? cell_hi(cx) : cell_lo(cx)), p.x);
+    const float ay = __fsub_rn(line_at<kShared>(g, 1, d.y > 0.0f ? cell_hi(cy) : cell_lo(cy)), p.y);
+    const float az = __fsub_rn(line_at<kShared>(g, 2, d.z > 0.0f ? cell_hi(cz) : cell_lo(cz)), p.z);
+    const float qx = vx ? __fdividef(ax, d.x) : inf;
+    const float qy = vy ? __fdividef(ay, d.y) : inf;
+    const float qz = vz ? __fdividef(az, d.z) : inf;
+    const float qm = fminf(fminf(qx, qy), qz);
+    // no valid axis, or an infinite / NaN quotient on every valid one: the reference keeps 1000
+    if (!(qm < inf)) return kOutside;
+    const bool sx = qx == qm, sy = !sx && qy == qm;
+    float t = __fdiv_rn(sx ? ax : (sy ? ay : az), sx ? d.x : (sy ? d.y : d.z));
+    const float lim = __fmul_rn(qm, 1.0f + 0x1p-19f);
+    const bool ox = !sx && qx <= lim, oy = !sy && qy <= lim, oz = (sx || sy) && qz <= lim;
+    if (ox || oy || oz) {  // near tie
+        if (ox) t = fminf(t, __fdiv_rn(ax, d.x));
+        if (oy) t = fminf(t, __fdiv_rn(ay, d.y));
+        if (oz) t = fminf(t, __fdiv_rn(az, d.z));
+    }
+    return fmaxf(fminf(t, kOutside), kVoidAdvance);
 }
 
 // Claim rays for the idle lanes of the warp: returns this lane's new ray or ~0u.
@@ -937,7 +940,7 @@ struct SceneAccess<true> {
 };
 
 template <bool kFan, bool kMulti, int kLevels>
-__global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(const TraceArgs a)
+__global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -955,19 +958,21 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
         S.bn_ = bn;
         S.sc_ = make_float3(a.scene.scale[0], a.scene.scale[1], a.scene.scale[2]);
         S.g.n = 1 << a.scene.depth;
-        S.g.lines = s_lines;
+        S.g.lines = s_lines + 1;
         if (n_smem) {
             const uint4* src = reinterpret_cast<const uint4*>(a.scene.recs);
             uint4* dst = reinterpret_cast<uint4*>(s_recs);
             for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
         }
-        // grid lines by the midpoint rule, level by level
+        // grid lines by the midpoint rule, level by level, between the -inf / +inf sentinels
         const int n = S.g.n;
         if (threadIdx.x < 3) {
             const unsigned ax = threadIdx.x;
-            s_lines[ax * (n + 2)] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
-            s_lines[ax * (n + 2) + n] = ax == 0 ? bn.x : (ax == 1 ? bn.y : bn.z);
-            s_lines[ax * (n + 2) + n + 1] = __int_as_float(0x7f800000);
+            float* row = s_lines + ax * line_row(n);
+            row[0] = -__int_as_float(0x7f800000);
+            row[1] = ax == 0 ? b0.x : (ax == 1 ? b0.y : b0.z);
+            row[n + 1] = ax == 0 ? bn.x : (ax == 1 ? bn.y : bn.z);
+            row[n + 2] = __int_as_float(0x7f800000);
         }
         __syncthreads();
         for (int lvl = 0; lvl < a.scene.depth; ++lvl) {
@@ -976,7 +981,7 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
             for (int w = threadIdx.x; w < 3 * cells; w += blockDim.x) {
                 const int axis = w / cells;
                 const int c = w - axis * cells;
-                float* row = s_lines + axis * (n + 2);
+                float* row = s_lines + axis * line_row(n) + 1;
                 row[c * stride + (stride >> 1)] = (row[c * stride] + row[c * stride + stride]) * 0.5f;
             }
             __syncthreads();
@@ -1041,12 +1046,12 @@ __global__ void __launch_bounds__(kThreads, kMulti ? 4 : 1) trace_grid_kernel(co
         if (!(flags & kInDesc)) {
             // ---- start of a march step (kernel.cu:260-294) ----
             const GridView g = S.grid();
-            const float3 b0 = S.b0(), bn = S.bn(), scale = S.scale();
+            const float3 b0 = S.b0(), scale = S.scale();
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
             bool ex, ey, ez;
-            const int ix = grid_index<kShared>(g, 0, p.x, b0.x, bn.x, scale.x, ex);
-            const int iy = grid_index<kShared>(g, 1, p.y, b0.y, bn.y, scale.y, ey);
-            const int iz = grid_index<kShared>(g, 2, p.z, b0.z, bn.z, scale.z, ez);
+            const int ix = grid_index<kShared>(g, 0, p.x, b0.x, scale.x, ex);
+            const int iy = grid_index<kShared>(g, 1, p.y, b0.y, scale.y, ey);
+            const int iz = grid_index<kShared>(g, 2, p.z, b0.z, scale.z, ez);
             if ((flags & kVoidOk) && cell_open(vcx, ix, ex) && cell_open(vcy, iy, ey) && cell_open(vcz, iz, ez)) {
                 flags |= kNeedExit;  // exit distance below, with the descents that end in a void cell
                 step_done = true;
@@ -1361,7 +1366,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     if (kind == Kind::kGrid) {
         kern = trace_grid_kernel<kFan, kMulti, 3>;
         base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
-        if (!kMulti) base += 3u * ((static_cast<size_t>(1) << a.scene.depth) + 2u) * 4u;
+        if (!kMulti) base += 3u * static_cast<size_t>(line_row(1 << a.scene.depth)) * 4u;
     } else {
         kern = trace_float_kernel<kFan, kMulti>;
         base = 0;

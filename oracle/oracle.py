@@ -47,6 +47,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_half_to_float.restype = ctypes.c_float
         L.oracle_half_to_float.argtypes = [ctypes.c_uint16]
         L.oracle_num_threads.restype = ctypes.c_int
+        L.oracle_trace_mix.restype = ctypes.c_int64
+        L.oracle_trace_mix.argtypes = [vp, ctypes.c_uint64, vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int,
+                                       ctypes.c_float, ctypes.c_float, ctypes.c_int, vp]
         _lib = L
     return _lib
 
@@ -90,6 +93,27 @@ def trace(
     if rc != 0:
         raise RuntimeError(f"oracle: DAG index outside the payload on ray {-rc - 1}")
     return {"dist": dist, "sem": sem, "steps": steps, "loads": loads}
+
+
+MIX_NAMES = ("steps", "void_cache", "outside", "leaf_cache", "descents", "descent_leaf", "descent_void", "levels")
+
+
+def step_mix(words: np.ndarray, bbox_min, bbox_max, origins: np.ndarray, dirs: np.ndarray, *, max_steps: int,
+             max_distance: float, hit_epsilon: float = 0.01, threads: int = 0) -> dict[str, int]:
+    """What the reference algorithm's march steps did, summed over the rays (fused position update):
+    steps, void-cache hits, steps outside the box, leaf-cache hits, descents, descents ending in a
+    leaf / an empty octant, and descent levels."""
+    w = np.ascontiguousarray(np.asarray(words).view(np.uint64))
+    o = _f32(origins).reshape(-1, 3)
+    d = _f32(dirs).reshape(-1, 3)
+    bmin = _f32(bbox_min).reshape(3)
+    bmax = _f32(bbox_max).reshape(3)
+    mix = np.zeros(len(MIX_NAMES), np.int64)
+    rc = lib().oracle_trace_mix(_ptr(w), w.shape[0], _ptr(bmin), _ptr(bmax), _ptr(o), _ptr(d), o.shape[0],
+                                int(max_steps), float(max_distance), float(hit_epsilon), int(threads), _ptr(mix))
+    if rc != 0:
+        raise RuntimeError(f"oracle: DAG index outside the payload on ray {-rc - 1}")
+    return {k: int(v) for k, v in zip(MIX_NAMES, mix)}
 
 
 def point_query(words: np.ndarray, bbox_min, bbox_max, p) -> tuple[float, int]:

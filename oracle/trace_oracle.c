@@ -131,20 +131,27 @@ static int load_word(const dag_view *v, uint32_t ptr, uint64_t *out, int64_t *lo
     return 0;
 }
 
+/* Step mix (optional, oracle_trace_mix): what each march step of the reference did. */
+enum { MIX_STEPS, MIX_VOID_CACHE, MIX_OUTSIDE, MIX_LEAF_CACHE, MIX_DESCENTS, MIX_DESC_LEAF, MIX_DESC_VOID,
+       MIX_LEVELS, MIX_N };
+
 /* kernel.cu:88-200.  Returns 0, or -1 on an index outside the payload. */
 static int query(const dag_view *v, float px, float py, float pz, float dx, float dy, float dz,
-                 ray_caches *c, float *out_dist, int32_t *out_sem, int64_t *loads)
+                 ray_caches *c, float *out_dist, int32_t *out_sem, int64_t *loads, int64_t *mix)
 {
     if (!in_closed(px, py, pz, v->mn, v->mx)) {
+        if (mix) mix[MIX_OUTSIDE]++;
         *out_dist = OR_OUTSIDE_DOMAIN;
         *out_sem = 0;
         return 0;
     }
     if (c->leaf_valid && in_closed(px, py, pz, c->leaf_mn, c->leaf_mx)) {
+        if (mix) mix[MIX_LEAF_CACHE]++;
         *out_dist = c->leaf_dist;
         *out_sem = c->leaf_sem;
         return 0;
     }
+    if (mix) mix[MIX_DESCENTS]++;
     const int use_prefix = c->pre_valid && in_closed(px, py, pz, c->pre_mn, c->pre_mx);
     uint32_t ptr = use_prefix ? c->pre_ptr : 0u;
     float mn[3], mx[3];
@@ -155,8 +162,10 @@ static int query(const dag_view *v, float px, float py, float pz, float dx, floa
     int depth = use_prefix ? OR_PREFIX_DEPTH : 0;
     for (; depth < OR_MAX_DEPTH; ++depth) {
         uint64_t node;
+        if (mix) mix[MIX_LEVELS]++;
         if (load_word(v, ptr, &node, loads)) return -1;
         if ((node >> 63) == 1) {
+            if (mix) mix[MIX_DESC_LEAF]++;
             for (int a = 0; a < 3; ++a) {
                 c->leaf_mn[a] = mn[a];
                 c->leaf_mx[a] = mx[a];
@@ -190,6 +199,7 @@ static int query(const dag_view *v, float px, float py, float pz, float dx, floa
                 c->void_mx[a] = mx[a];
             }
             c->void_valid = 1;
+            if (mix) mix[MIX_DESC_VOID]++;
             *out_dist = exit_distance(px, py, pz, dx, dy, dz, c->void_mn, c->void_mx);
             *out_sem = 0;
             return 0;
@@ -215,7 +225,7 @@ typedef struct {
 /* kernel.cu:203-309 for one ray */
 static ray_result trace_one(const dag_view *v, float ox, float oy, float oz, float dx, float dy,
                             float dz, int max_steps, float max_distance, float hit_eps,
-                            int use_fma)
+                            int use_fma, int64_t *mix)
 {
     ray_result r = {0.0f, 0, 0, 0, 0};
     ray_caches c;
@@ -235,10 +245,12 @@ static ray_result trace_one(const dag_view *v, float ox, float oy, float oz, flo
             py = oy + t * dy;
             pz = oz + t * dz;
         }
+        if (mix) mix[MIX_STEPS]++;
         if (c.void_valid && in_open(px, py, pz, c.void_mn, c.void_mx)) {
+            if (mix) mix[MIX_VOID_CACHE]++;
             dist = exit_distance(px, py, pz, dx, dy, dz, c.void_mn, c.void_mx);
             sem = 0;
-        } else if (query(v, px, py, pz, dx, dy, dz, &c, &dist, &sem, &r.loads)) {
+        } else if (query(v, px, py, pz, dx, dy, dz, &c, &dist, &sem, &r.loads, mix)) {
             r.err = 1;
             return r;
         }
@@ -288,7 +300,7 @@ int64_t oracle_trace(const uint64_t *dag, uint64_t n_words, const float *bmin, c
         const float *o = origins + 3 * i;
         const float *d = dirs + 3 * i;
         ray_result r = trace_one(&v, o[0], o[1], o[2], d[0], d[1], d[2], max_steps, max_distance,
-                                 hit_eps, use_fma);
+                                 hit_eps, use_fma, NULL);
         out_dist[i] = r.t;
         out_sem[i] = r.sem;
         if (out_steps) out_steps[i] = r.steps;
@@ -299,6 +311,55 @@ int64_t oracle_trace(const uint64_t *dag, uint64_t n_words, const float *bmin, c
 #endif
             if (first_err == 0 || -(i + 1) > first_err) first_err = -(i + 1);
         }
+    }
+    return first_err;
+}
+
+/*
+ * Step mix of the reference algorithm over n_rays rays: mix[8] receives the number of
+ * march steps, void-cache hits (kernel.cu:265), steps outside the box (:108), leaf-cache
+ * hits (:114), descents, descents ending in a leaf (:139) and in an empty octant (:178),
+ * and descent levels (node words loaded at :137).  Returns 0 or the negative index of
+ * the first ray that met an index outside the payload.
+ */
+int64_t oracle_trace_mix(const uint64_t *dag, uint64_t n_words, const float *bmin, const float *bmax,
+                         const float *origins, const float *dirs, int64_t n_rays, int max_steps,
+                         float max_distance, float hit_eps, int n_threads, int64_t *mix)
+{
+    dag_view v;
+    v.dag = dag;
+    v.n = n_words;
+    for (int a = 0; a < 3; ++a) {
+        v.mn[a] = bmin[a];
+        v.mx[a] = bmax[a];
+    }
+    for (int k = 0; k < MIX_N; ++k) mix[k] = 0;
+    int64_t first_err = 0;
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+#pragma omp parallel
+#endif
+    {
+        int64_t local[MIX_N] = {0};
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 64)
+#endif
+        for (int64_t i = 0; i < n_rays; ++i) {
+            const float *o = origins + 3 * i;
+            const float *d = dirs + 3 * i;
+            ray_result r = trace_one(&v, o[0], o[1], o[2], d[0], d[1], d[2], max_steps, max_distance, hit_eps, 1,
+                                     local);
+            if (r.err) {
+#ifdef _OPENMP
+#pragma omp critical
+#endif
+                if (first_err == 0 || -(i + 1) > first_err) first_err = -(i + 1);
+            }
+        }
+#ifdef _OPENMP
+#pragma omp critical
+#endif
+        for (int k = 0; k < MIX_N; ++k) mix[k] += local[k];
     }
     return first_err;
 }
@@ -320,7 +381,7 @@ int oracle_point_query(const uint64_t *dag, uint64_t n_words, const float *bmin,
     int64_t loads = 0;
     *out_dist = 0.0f;
     *out_sem = 0;
-    return query(&v, px, py, pz, 1.0f, 0.0f, 0.0f, &c, out_dist, out_sem, &loads);
+    return query(&v, px, py, pz, 1.0f, 0.0f, 0.0f, &c, out_dist, out_sem, &loads, NULL);
 }
 
 int oracle_num_threads(void)
