@@ -640,7 +640,6 @@ constexpr int kStackLevels = tsdf::kMaxGridDepth;
 constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
 constexpr uint32_t kNeedExit = 64u;      // step ended in the void cell: exit distance still to compute
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
-constexpr int kLvShift = 16;             // 6 bits: level of the node being descended
 
 // A cell of the finest grid's units: lo | size << 16 (size = 2^shift <= 4096).
 __device__ __forceinline__ uint32_t pack_cell(int j, int shift)
@@ -939,15 +938,16 @@ struct SceneAccess<true> {
     __device__ __forceinline__ float3 scale() const { return make_float3(__ldg(&s->scale[0]), __ldg(&s->scale[1]), __ldg(&s->scale[2])); }
 };
 
-template <bool kFan, bool kMulti, int kLevels>
-__global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs a)
+// kMinBlocks: resident blocks per SM the register allocation is held to (4: up to 64
+// registers; 5: 48, with a few spill slots).  Five blocks hide more latency and pay off
+// on long launches; on short ones the extra resident warps lengthen the tail.
+template <bool kFan, bool kMulti, int kLevels, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint32_t* s_stack = reinterpret_cast<uint32_t*>(smem_raw);   // [kStackLevels][kThreads]
-    uint32_t* s_recs = s_stack + kStackLevels * kThreads;           // [n_smem][8]
-    const uint32_t n_smem = kMulti ? 0u : a.n_smem;
-    float* s_lines = reinterpret_cast<float*>(s_recs + 8u * n_smem);  // [3][2^D + 2]
+    float* s_lines = reinterpret_cast<float*>(s_stack + kStackLevels * kThreads);  // [3][line_row(2^D)]
 
     SceneAccess<kMulti> S;
     S.s = kMulti ? a.table : &a.scene;
@@ -959,11 +959,6 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
         S.sc_ = make_float3(a.scene.scale[0], a.scene.scale[1], a.scene.scale[2]);
         S.g.n = 1 << a.scene.depth;
         S.g.lines = s_lines + 1;
-        if (n_smem) {
-            const uint4* src = reinterpret_cast<const uint4*>(a.scene.recs);
-            uint4* dst = reinterpret_cast<uint4*>(s_recs);
-            for (uint32_t i = threadIdx.x; i < 2u * n_smem; i += blockDim.x) dst[i] = __ldg(src + i);
-        }
         // grid lines by the midpoint rule, level by level, between the -inf / +inf sentinels
         const int n = S.g.n;
         if (threadIdx.x < 3) {
@@ -1015,6 +1010,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
     float leaf_d = 0.f;
     int32_t leaf_s = 0;
     uint32_t pre_rec = 0, node = 0;
+    int lvl = 0;  // level of `node` in the descent under way
 
     for (;;) {
         const uint32_t mine = claim_ray(q_next, q_end, exhausted, active, lane, a.counter, a.chunk, n_work);
@@ -1100,62 +1096,64 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                     if (use_pre) flags |= kSvHigh;
                     else flags &= ~kSvHigh;
                 }
-                flags = (flags & ~((63u << kLvShift) | kUsePre)) | kInDesc | (use_pre ? kUsePre : 0u) |
-                        (static_cast<uint32_t>(level) << kLvShift);
+                flags = (flags & ~kUsePre) | kInDesc | (use_pre ? kUsePre : 0u);
+                lvl = level;
             }
         }
 #pragma unroll 1
         for (int it = 0; it < kLevels && (flags & kInDesc); ++it) {
             // ---- one descent level (kernel.cu:136-198) ----
-            int level = static_cast<int>((flags >> kLvShift) & 63u);
             uint32_t leaf = 0;
-            int leaf_level = level;
+            int leaf_level = lvl;
             bool is_leaf = false;
             bool done = false;
-            if (node & tsdf::kSlotLeafBit) {
-                leaf = node & ~tsdf::kSlotLeafBit;
-                is_leaf = true;
-            } else if (node & tsdf::kSlotExtBit) {
-                if (checked(a.err, (node & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable))
+            if (node >= tsdf::kSlotExtBit) {
+                // a leaf slot as the descent's start node: the root of a one-leaf DAG
+                if (node & tsdf::kSlotLeafBit) {
+                    leaf = node & ~tsdf::kSlotLeafBit;
+                } else if (checked(a.err, (node & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable)) {
                     leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
                                                        (node & tsdf::kSlotIndexMask)));
+                }
                 is_leaf = true;
             } else {
-                if (checked(a.err, level < kStackLevels, kErrStack)) my_stack[level * kThreads] = node;
-                if (level == kPrefixDepth && !(flags & kUsePre)) {
+                if (checked(a.err, lvl < kStackLevels, kErrStack)) my_stack[lvl * kThreads] = node;
+                if (lvl == kPrefixDepth && !(flags & kUsePre)) {
                     pre_rec = node;
                     pcx = pack_cell(jx, D - kPrefixDepth);
                     pcy = pack_cell(jy, D - kPrefixDepth);
                     pcz = pack_cell(jz, D - kPrefixDepth);
                     flags |= kPreOk;
                 }
-                const int sh = D - 1 - level;
+                const int sh = D - 1 - lvl;
                 const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
-                const size_t si = static_cast<size_t>(node) * 8u + oct;
                 uint32_t slot = tsdf::kSlotVoid;
                 if (checked(a.err, node < S.n_recs(), kErrRecord))
-                    slot = (node < n_smem) ? s_recs[si] : __ldg(S.recs() + si);
-                leaf_level = level + 1;
+                    slot = __ldg(S.recs() + (static_cast<size_t>(node) * 8u + oct));
+                leaf_level = lvl + 1;
+                // A record graph of height D <= 12 ends every path by level D, so the
+                // reference's 32-level cap (kernel.cu:136) is never reached here.
                 if (slot == tsdf::kSlotVoid) {
-                    vcx = pack_cell(jx, D - leaf_level);
-                    vcy = pack_cell(jy, D - leaf_level);
-                    vcz = pack_cell(jz, D - leaf_level);
+                    const uint32_t keep = 0xFFFFu << sh, size = 1u << (sh + 16);  // cells of side 2^sh
+                    vcx = (static_cast<uint32_t>(jx) & keep) | size;
+                    vcy = (static_cast<uint32_t>(jy) & keep) | size;
+                    vcz = (static_cast<uint32_t>(jz) & keep) | size;
                     flags |= kVoidOk | kNeedExit;
                     done = true;
-                } else if (leaf_level >= kMaxDepth) {
-                    done = true;  // cap reached: dist / sem keep their previous values
                 } else if (slot & tsdf::kSlotLeafBit) {
                     leaf = slot & ~tsdf::kSlotLeafBit;
                     is_leaf = true;
                 } else {
                     node = slot;
-                    flags = (flags & ~(63u << kLvShift)) | (static_cast<uint32_t>(leaf_level) << kLvShift);
+                    lvl = leaf_level;
                 }
             }
             if (is_leaf) {
-                lcx = pack_cell(jx, D - leaf_level);
-                lcy = pack_cell(jy, D - leaf_level);
-                lcz = pack_cell(jz, D - leaf_level);
+                const int sh = D - leaf_level;
+                const uint32_t keep = 0xFFFFu << sh, size = 1u << (sh + 16);
+                lcx = (static_cast<uint32_t>(jx) & keep) | size;
+                lcy = (static_cast<uint32_t>(jy) & keep) | size;
+                lcz = (static_cast<uint32_t>(jz) & keep) | size;
                 leaf_d = leaf_distance(leaf);
                 leaf_s = static_cast<int32_t>(leaf >> 16);
                 flags |= kLeafOk;
@@ -1364,7 +1362,15 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
     void (*kern)(TraceArgs);
     size_t base;  // shared memory besides the staged records
     if (kind == Kind::kGrid) {
-        kern = trace_grid_kernel<kFan, kMulti, 3>;
+        // the grid kernel reads records through L1 (staging the top records in shared
+        // memory measured slower on every configuration); option smem_records applies to
+        // the float kernel only
+        a.n_smem = 0;
+        // five resident blocks for the per-scene launches of scene tables and launches of
+        // 2^21 rays or more (configs 3-5: +3 %), four below (config 2: 5 % faster than five)
+        const bool long_launch = a.seg != nullptr || a.n_rays >= (1u << 21);
+        if constexpr (kMulti) kern = trace_grid_kernel<kFan, kMulti, 3, 4>;
+        else kern = long_launch ? trace_grid_kernel<kFan, kMulti, 3, 5> : trace_grid_kernel<kFan, kMulti, 3, 4>;
         base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
         if (!kMulti) base += 3u * static_cast<size_t>(line_row(1 << a.scene.depth)) * 4u;
     } else {
