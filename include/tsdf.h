@@ -209,8 +209,9 @@ TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, cons
                                const float bbox_max[3], float hit_epsilon, void* stream);
 
 /* Tuning knobs (process-wide): "smem_records" (top records staged in shared
- * memory per block, default 0: on sm_100 the L1 serves them as fast; capped so
- * the block keeps its register-limited occupancy), "chunk" (rays a warp claims
+ * memory per block by the float-descent kernel, default 0: on sm_100 the L1 serves
+ * them as fast; capped so the block keeps its register-limited occupancy; the grid
+ * kernel always reads records through L1), "chunk" (rays a warp claims
  * at once; default 0 = per launch: 32 for the per-scene launches of scene tables
  * and for launches of 2^21 rays or more, else 8), "leaf_run" (leaf-cache steps a single-scene lane takes in
  * place after a step, default 1), "blocks_per_sm" (0 = occupancy maximum),
