@@ -726,7 +726,7 @@ def _e2e_fan(torch, wl: FanWorkload, args, flush) -> dict:
         torch.cuda.synchronize(wl.dev)
         ms.append(s0.elapsed_time(e0))
     return {"value": n / (float(np.mean(ms)) / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(a * 32),
-            "d2h_bytes_per_step": int(n * 12),
+            "d2h_bytes_per_step": int(n * 12), "ms_per_step": float(np.mean(ms)), "rays_per_step": n,
             "api": "navi_b200.pipeline.cast_fan_host (host poses in, dist/sem/steps out, 4 chunks overlapped)"}
 
 
@@ -784,13 +784,16 @@ def run_navi(args) -> None:
 
     # explicit-ray kernel on the same rays (the drop-in cast_rays path), device-resident; one scene only
     explicit = None if len(wl.scene_list) != 1 else _explicit(torch, wl, args, flush, stream)
-    observe =None if args.no_e2e else _observe(torch, wl, args, flush)
+    observe = None if args.no_e2e else _observe(torch, wl, args, flush)
     e2e, e2e_rays, e2e_ms = (None, 0.0, 0.0) if args.no_e2e else _e2e(torch, wl, args, flush, dist)
     e2e_fan = None if args.no_e2e else _e2e_fan(torch, wl, args, flush)
 
-    # gather per-rank [rays, ms, steps, e2e rays, e2e ms] over NCCL; job time = max over ranks
-    stats = torch.tensor([float(wl.n * args.steps), my_ms, steps_mean, e2e_rays, e2e_ms], dtype=torch.float64,
-                         device=dev)
+    # gather per-rank [rays, ms, steps, e2e rays, e2e ms, fan e2e rays, fan e2e ms] over NCCL;
+    # every job time is the max over ranks
+    fan_rays = float(e2e_fan["rays_per_step"]) if e2e_fan else 0.0
+    fan_ms = float(e2e_fan["ms_per_step"]) if e2e_fan else 0.0
+    stats = torch.tensor([float(wl.n * args.steps), my_ms, steps_mean, e2e_rays, e2e_ms, fan_rays, fan_ms],
+                         dtype=torch.float64, device=dev)
     table = dist_stats.gather_rank_stats(stats, dist)
     total_rays, job_ms = dist_stats.job_figures(table)
 
@@ -799,21 +802,31 @@ def run_navi(args) -> None:
         hbm, hbm_kind = _peaks()
         l2peak = _l2_read_peak(torch, dev)
         roof, cpu = None, None
-        if world == 1 and not args.no_cpu_baseline:
+        if not args.no_cpu_baseline:
             cores = os.cpu_count() or 8
             sample = args.cpu_sample_actors or max(1, min(wl.actors, 2 * cores))
             w_ref, cpu_rays_s, threads, used = _w_ref(cfg, wl.scene_list, wl.sets[0], wl.fan_np,
                                                       wl.poses[0].cpu().numpy(), sample)
-            cpu = {"value": cpu_rays_s, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{used} of {wl.actors} actors x {wl.r} rays (oracle/trace_oracle.c, the reference "
-                             f"kernel restated in C, OpenMP, {threads} threads)"}
-            roof = _roofline(wl.n, step_ms, w_ref, hbm, hbm_kind, l2peak, _traffic(cfg.name))
+            if world == 1:  # the CPU baseline is reported at N=1 only
+                cpu = {"value": cpu_rays_s, "unit": UNIT, "cores": threads, "kind": "port",
+                       "sample": f"{used} of {wl.actors} actors x {wl.r} rays (oracle/trace_oracle.c, the reference "
+                                 f"kernel restated in C, OpenMP, {threads} threads)"}
+            # per GPU: this rank's rays over the slowest rank's step time
+            roof = _roofline(wl.n, [job_ms / args.steps], w_ref, hbm, hbm_kind, l2peak,
+                             _traffic(cfg.name) if world == 1 else None)
+            if world > 1:
+                roof["scope"] = f"per GPU: one rank's rays over the slowest of {world} ranks' mean step time"
         value = total_rays / (job_ms / 1e3)
         if e2e is not None:
             e2e = dict(e2e)
             e2e["value"] = float(table[:, 3].sum()) / (float(table[:, 4].max()) / 1e3)
             if world > 1:
                 e2e["scope"] = f"box: rays of all {world} ranks over the slowest rank's mean step time"
+        if e2e_fan is not None:
+            e2e_fan = dict(e2e_fan)
+            e2e_fan["value"] = float(table[:, 5].sum()) / (float(table[:, 6].max()) / 1e3)
+            if world > 1:
+                e2e_fan["scope"] = f"box: rays of all {world} ranks over the slowest rank's mean step time"
         line = {
             "metric": METRIC,
             "value": value,
