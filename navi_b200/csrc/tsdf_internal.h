@@ -82,7 +82,7 @@ struct tsdf_pool {
 struct TsdfSceneDev {
     const uint32_t* recs;
     const uint64_t* ext;
-    const float* lines;              // [3][2^depth + 2] grid lines, or null (float descent)
+    const float* lines;              // B[0] of 3 rows of -inf, B[0..2^depth], +inf, or null (float descent)
     uint32_t root;
     uint32_t n_recs;
     float bmin[3];
@@ -91,8 +91,9 @@ struct TsdfSceneDev {
     int32_t depth;                   // grid depth D (cells per axis 2^D); -1: float descent
     float scale[3];                  // 2^D / (bmax - bmin) per axis, float division
     uint32_t n_ext;                  // out-of-line leaves (bounds-checked builds)
+    float offs[3];                   // -(bmin * scale) per axis: cell estimate u = fma(p, scale, offs)
 };
-static_assert(sizeof(TsdfSceneDev) == 80, "scene record layout");
+static_assert(sizeof(TsdfSceneDev) == 96, "scene record layout");
 
 struct tsdf_scenes {
     int device = 0;
@@ -105,12 +106,16 @@ struct tsdf_scenes {
 
 namespace tsdf {
 // Cells per unit length along each axis, 2^D / (bmax - bmin), each an IEEE float
-// subtraction and division (the same values the device's __fsub_rn / __fdiv_rn give).
+// subtraction and division (the same values the device's __fsub_rn / __fdiv_rn give),
+// and the offset of the cell estimate u(p) = fma(p, scale, offs), offs = -(bmin * scale)
+// rounded once; build_grid_lines proves the estimate's one-cell bound with the same values.
+inline float grid_scale(float lo, float hi, int depth) { return static_cast<float>(1 << depth) / (hi - lo); }
+inline float grid_offset(float lo, float scale) { return -(lo * scale); }
 inline void set_grid_scale(TsdfSceneDev& d)
 {
     for (int a = 0; a < 3; ++a) {
-        const float ext = d.bmax[a] - d.bmin[a];
-        d.scale[a] = d.depth >= 0 ? static_cast<float>(1 << d.depth) / ext : 0.0f;
+        d.scale[a] = d.depth >= 0 ? grid_scale(d.bmin[a], d.bmax[a], d.depth) : 0.0f;
+        d.offs[a] = d.depth >= 0 ? grid_offset(d.bmin[a], d.scale[a]) : 0.0f;
     }
 }
 void set_error(const std::string& msg);

@@ -249,12 +249,14 @@ bool build_grid_lines(float lo, float hi, int depth, float* out)
     }
     for (int k = 0; k < n; ++k)
         if (!(out[k] < out[k + 1])) return false;
-    // The kernel estimates the cell of p as floor(u(p)), u(p) = RN(RN(p - lo) * scale) with
-    // scale = RN(n / RN(hi - lo)), and then picks among cells e-1, e, e+1.  u is monotone in p,
-    // so |u(out[k]) - k| < 1 for every line k bounds the estimate within one cell everywhere.
-    const float scale = static_cast<float>(n) / (hi - lo);
+    // The kernel estimates the cell of p as floor(u(p)), u(p) = RN(p * scale + offs) (one
+    // fused multiply-add) with scale = RN(n / RN(hi - lo)) and offs = -RN(lo * scale), and then
+    // picks among cells e-1, e, e+1.  u is monotone in p (scale > 0), so |u(out[k]) - k| < 1
+    // for every line k bounds the estimate within one cell everywhere.
+    const float scale = grid_scale(lo, hi, depth);
+    const float offs = grid_offset(lo, scale);
     for (int k = 0; k <= n; ++k) {
-        const float u = (out[k] - lo) * scale;
+        const float u = std::fma(out[k], scale, offs);
         if (!(std::fabs(u - static_cast<float>(k)) < 1.0f)) return false;
     }
     return true;

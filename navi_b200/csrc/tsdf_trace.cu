@@ -682,13 +682,14 @@ __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
 
 // Index of the last grid line <= p: -1 below the box, n at or above its top face (n + 1
 // for p = +inf, which every later test treats as outside), and whether p lies on it.
-// e = floor(u(p)), clamped to [0, n], is within one cell of the answer (proved per table
-// on the host, build_grid_lines), so three neighbouring lines decide it; the -inf / +inf
+// e = floor(u(p)), u(p) = fma(p, scale, offs), clamped to [0, n], is within one cell of
+// the answer (proved per table on the host, build_grid_lines), so three neighbouring lines
+// decide it; the -inf / +inf
 // sentinels at both ends of the row make the box faces need no special case (NaN: -1).
 template <bool kShared>
-__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float b0, float scale, bool& on)
+__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float scale, float offs, bool& on)
 {
-    const int e = max(min(__float2int_rz(__fmul_rn(__fsub_rn(p, b0), scale)), g.n), 0);
+    const int e = max(min(__float2int_rz(__fmaf_rn(p, scale, offs)), g.n), 0);
     const float lm = line_at<kShared>(g, axis, e - 1);
     const float l0 = line_at<kShared>(g, axis, e);
     const float lp = line_at<kShared>(g, axis, e + 1);
@@ -697,24 +698,31 @@ __device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, 
     return e - 1 + (ge0 ? 1 : 0) + (gep ? 1 : 0);
 }
 
+// Per-axis reciprocals of a ray's direction, correctly rounded, for the approximate exit
+// quotients (a * RN(1/d) is within 2^-22 relative of a / d); NaN where |d| <= 1e-4, the
+// axes kernel.cu:54-85 leaves out.  Kept per lane in shared memory while the ray lives.
+__device__ __forceinline__ float axis_reciprocal(float dv)
+{
+    return fabsf(dv) > kDirEps ? __frcp_rn(dv) : __int_as_float(0x7fc00000);
+}
+
 // kernel.cu:54-85 with the void cell's faces read from the grid lines.  Approximate
 // quotients (within 2^-21 relative of the exact ones) pick the axis of the minimum, which
 // alone gets the IEEE division: one division per lane, so a warp whose lanes leave their
 // cells through different faces runs one division sequence, not three.  Axes whose
 // approximate quotient lies within the approximation margin of the minimum (a near tie,
 // rare) get their IEEE division too, so the result is the reference's min over axes.
+// rcp: the lane's per-axis reciprocals of d (ray_reciprocals), NaN on the axes the
+// reference skips (|d| <= 1e-4), whose quotients then drop out of every comparison.
 template <bool kShared>
 __device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
-                                                    uint32_t cx, uint32_t cy, uint32_t cz)
+                                                    const float3 rcp, uint32_t cx, uint32_t cy, uint32_t cz)
 {
     const float inf = __int_as_float(0x7f800000);
-    const bool vx = fabsf(d.x) > kDirEps, vy = fabsf(d.y) > kDirEps, vz = fabsf(d.z) > kDirEps;
     const float ax = __fsub_rn(line_at<kShared>(g, 0, d.x > 0.0f ? cell_hi(cx) : cell_lo(cx)), p.x);
     const float ay = __fsub_rn(line_at<kShared>(g, 1, d.y > 0.0f ? cell_hi(cy) : cell_lo(cy)), p.y);
     const float az = __fsub_rn(line_at<kShared>(g, 2, d.z > 0.0f ? cell_hi(cz) : cell_lo(cz)), p.z);
-    const float qx = vx ? __fdividef(ax, d.x) : inf;
-    const float qy = vy ? __fdividef(ay, d.y) : inf;
-    const float qz = vz ? __fdividef(az, d.z) : inf;
+    const float qx = __fmul_rn(ax, rcp.x), qy = __fmul_rn(ay, rcp.y), qz = __fmul_rn(az, rcp.z);
     const float qm = fminf(fminf(qx, qy), qz);
     // no valid axis, or an infinite / NaN quotient on every valid one: the reference keeps 1000
     if (!(qm < inf)) return kOutside;
@@ -896,7 +904,7 @@ template <>
 struct SceneAccess<false> {
     const TsdfSceneDev* s;
     GridView g;
-    float3 b0_, bn_, sc_;
+    float3 b0_, bn_, sc_, of_;
     __device__ __forceinline__ const uint32_t* recs() const { return s->recs; }
     __device__ __forceinline__ const uint64_t* ext() const { return s->ext; }
     __device__ __forceinline__ uint32_t root() const { return s->root; }
@@ -908,6 +916,7 @@ struct SceneAccess<false> {
     __device__ __forceinline__ float3 b0() const { return b0_; }
     __device__ __forceinline__ float3 bn() const { return bn_; }
     __device__ __forceinline__ float3 scale() const { return sc_; }
+    __device__ __forceinline__ float3 offs() const { return of_; }
 };
 
 template <>
@@ -936,6 +945,7 @@ struct SceneAccess<true> {
     __device__ __forceinline__ float3 b0() const { return make_float3(__ldg(&s->bmin[0]), __ldg(&s->bmin[1]), __ldg(&s->bmin[2])); }
     __device__ __forceinline__ float3 bn() const { return make_float3(__ldg(&s->bmax[0]), __ldg(&s->bmax[1]), __ldg(&s->bmax[2])); }
     __device__ __forceinline__ float3 scale() const { return make_float3(__ldg(&s->scale[0]), __ldg(&s->scale[1]), __ldg(&s->scale[2])); }
+    __device__ __forceinline__ float3 offs() const { return make_float3(__ldg(&s->offs[0]), __ldg(&s->offs[1]), __ldg(&s->offs[2])); }
 };
 
 // kMinBlocks: resident blocks per SM the register allocation is held to (4: up to 64
@@ -947,7 +957,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
     constexpr bool kShared = !kMulti;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint32_t* s_stack = reinterpret_cast<uint32_t*>(smem_raw);   // [kStackLevels][kThreads]
-    float* s_lines = reinterpret_cast<float*>(s_stack + kStackLevels * kThreads);  // [3][line_row(2^D)]
+    float* s_rcp = reinterpret_cast<float*>(s_stack + kStackLevels * kThreads);  // [3][kThreads]
+    float* s_lines = s_rcp + 3 * kThreads;                             // [3][line_row(2^D)]
 
     SceneAccess<kMulti> S;
     S.s = kMulti ? a.table : &a.scene;
@@ -957,6 +968,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
         S.b0_ = b0;
         S.bn_ = bn;
         S.sc_ = make_float3(a.scene.scale[0], a.scene.scale[1], a.scene.scale[2]);
+        S.of_ = make_float3(a.scene.offs[0], a.scene.offs[1], a.scene.offs[2]);
         S.g.n = 1 << a.scene.depth;
         S.g.lines = s_lines + 1;
         // grid lines by the midpoint rule, level by level, between the -inf / +inf sentinels
@@ -995,6 +1007,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
     }
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* my_stack = s_stack + threadIdx.x;
+    float* my_rcp = s_rcp + threadIdx.x;
     uint32_t q_next = 0, q_end = 0;
     bool exhausted = false;
 
@@ -1018,6 +1031,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
             int scene = 0;
             ray = work_ray<kFan, kMulti>(a, mine, seg_base);
             load_ray<kFan>(a, ray, o, d, scene);
+            my_rcp[0] = axis_reciprocal(d.x);
+            my_rcp[kThreads] = axis_reciprocal(d.y);
+            my_rcp[2 * kThreads] = axis_reciprocal(d.z);
             active = true;
             t = 0.f;
             dist = 0.f;
@@ -1042,12 +1058,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
         if (!(flags & kInDesc)) {
             // ---- start of a march step (kernel.cu:260-294) ----
             const GridView g = S.grid();
-            const float3 b0 = S.b0(), scale = S.scale();
+            const float3 scale = S.scale(), offs = S.offs();
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
             bool ex, ey, ez;
-            const int ix = grid_index<kShared>(g, 0, p.x, b0.x, scale.x, ex);
-            const int iy = grid_index<kShared>(g, 1, p.y, b0.y, scale.y, ey);
-            const int iz = grid_index<kShared>(g, 2, p.z, b0.z, scale.z, ez);
+            const int ix = grid_index<kShared>(g, 0, p.x, scale.x, offs.x, ex);
+            const int iy = grid_index<kShared>(g, 1, p.y, scale.y, offs.y, ey);
+            const int iz = grid_index<kShared>(g, 2, p.z, scale.z, offs.z, ez);
             if ((flags & kVoidOk) && cell_open(vcx, ix, ex) && cell_open(vcy, iy, ey) && cell_open(vcz, iz, ez)) {
                 flags |= kNeedExit;  // exit distance below, with the descents that end in a void cell
                 step_done = true;
@@ -1175,7 +1191,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
             // computed here once for both kinds of lanes (kernel.cu:54-85, :188)
             flags &= ~kNeedExit;
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
-            dist = cell_exit_distance<kShared>(S.grid(), p, d, vcx, vcy, vcz);
+            const float3 rcp = make_float3(my_rcp[0], my_rcp[kThreads], my_rcp[2 * kThreads]);
+            dist = cell_exit_distance<kShared>(S.grid(), p, d, rcp, vcx, vcy, vcz);
             sem = 0;
         }
         if (step_done) {
@@ -1371,7 +1388,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
         const bool long_launch = a.seg != nullptr || a.n_rays >= (1u << 21);
         if constexpr (kMulti) kern = trace_grid_kernel<kFan, kMulti, 3, 4>;
         else kern = long_launch ? trace_grid_kernel<kFan, kMulti, 3, 5> : trace_grid_kernel<kFan, kMulti, 3, 4>;
-        base = static_cast<size_t>(kStackLevels) * kThreads * 4u;
+        base = static_cast<size_t>(kStackLevels + 3) * kThreads * 4u;  // descent stack, reciprocals
         if (!kMulti) base += 3u * static_cast<size_t>(line_row(1 << a.scene.depth)) * 4u;
     } else {
         kern = trace_float_kernel<kFan, kMulti>;
