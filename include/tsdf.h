@@ -213,7 +213,7 @@ TSDF_API int tsdf_cast_noalloc(const tsdf_pool* pool, const float* origins, cons
  * them as fast; capped so the block keeps its register-limited occupancy; the grid
  * kernel always reads records through L1), "chunk" (rays a warp claims
  * at once; default 0 = per launch: 32 for the per-scene launches of scene tables
- * and for launches of 2^21 rays or more, else 8), "leaf_run" (leaf-cache steps a single-scene lane takes in
+ * and for launches of 2^21 rays or more, else 16), "leaf_run" (leaf-cache steps a single-scene lane takes in
  * place after a step, default 1), "blocks_per_sm" (0 = occupancy maximum),
  * "descent" (0 = integer grid descent wherever the DAG allows it, 1 = float
  * descent only), "order" (single-scene claim order: 1 = rays that can travel

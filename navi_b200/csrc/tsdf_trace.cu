@@ -663,7 +663,7 @@ __device__ __forceinline__ bool cell_open(uint32_t c, int i, bool on)
     return static_cast<uint32_t>(i - cell_lo(c)) - o < (c >> 16) - o;
 }
 
-// Per-axis grid lines: rows of kLineRow(n) = n + 3 floats, -inf, B[0..n], +inf; `lines`
+// Per-axis grid lines: rows of line_row(n) = n + 3 floats, -inf, B[0..n], +inf; `lines`
 // points at B[0] of axis 0, so line_at(axis, k) reads B[k] for k in [-1, n + 1].
 __host__ __device__ constexpr int line_row(int n) { return n + 3; }
 
@@ -1524,19 +1524,20 @@ void set_rpa_divisor(TraceArgs& a)
     a.rpa_shift = 31 + l;
 }
 
-// Rays a warp claims with one atomicAdd: option "chunk" when set, else 8 where the
+// Rays a warp claims with one atomicAdd: option "chunk" when set, else 16 where the
 // launch's tail is exposed and 32 where it is not.  Larger chunks mean fewer atomics and
 // longer runs of neighbouring rays per warp, but leave more claimed rays waiting in busy
 // warps while others sit idle at the end.  Per-scene launches overlap their ends with
 // the next launch on the other stream, and launches of 2^21 rays or more spend little of
-// their time in the tail (measured: config 2, 786k rays: 8 beats 32 by 6%; 1.6 M rays:
-// even; 4.2 M and 12.6 M rays: 32 wins 1.6% and 2.6%; per-scene launches of configs 3
-// and 5: 32 wins 1.4-1.6%).
+// their time in the tail (measured with lanes refilled in pairs: config 2, 786k rays: 16
+// beats 8, 4 and 64 by 1.7, 2.5 and 12 %; per-scene launches of config 5: 32 beats 16 and
+// 64 by 0.1 and 1.4 %; before the paired refill, 4.2 M and 12.6 M rays: 32 won 1.6 % and
+// 2.6 % over 8, and on config 2 8 beat 32 by 6 %).
 uint32_t pick_chunk(uint32_t n_rays, bool per_scene)
 {
     const int64_t c = g_chunk.load();
     if (c > 0) return static_cast<uint32_t>(c > 1024 ? 1024 : c);
-    return (per_scene || n_rays >= (1u << 21)) ? 32u : 8u;
+    return (per_scene || n_rays >= (1u << 21)) ? 32u : 16u;
 }
 
 // Scene tables of up to kMaxPerSceneLaunch scenes trace one single-scene launch per
