@@ -951,11 +951,11 @@ struct SceneAccess<true> {
     __device__ __forceinline__ float3 offs() const { return make_float3(__ldg(&s->offs[0]), __ldg(&s->offs[1]), __ldg(&s->offs[2])); }
 };
 
-// kMinBlocks: resident blocks per SM the register allocation is held to (4: up to 64
-// registers; 5: 48, with a few spill slots).  Five blocks hide more latency and pay off
-// on long launches; on short ones the extra resident warps lengthen the tail.
-template <bool kFan, bool kMulti, int kLevels, int kMinBlocks>
-__global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const TraceArgs a)
+// Four resident blocks of 256 per SM (up to 64 registers, no spills).  An instance held
+// to five blocks (48 registers, 24 bytes of spill slots) won 3 % on long launches before the
+// start of a step lost its branches, and lost 3.5 % on config 5 after.
+template <bool kFan, bool kMulti, int kLevels>
+__global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs a)
 {
     constexpr bool kShared = !kMulti;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1125,9 +1125,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
                 lvl = level;
             }
         }
-        // unrolled in the four-block instances (config 2: +1.3 %); the five-block ones,
-        // held to 48 registers, spill more when unrolled and stay rolled
-#pragma unroll (kMinBlocks == 4 ? kLevels : 1)
+#pragma unroll
         for (int it = 0; it < kLevels && (flags & kInDesc); ++it) {
             // ---- one descent level (kernel.cu:136-198) ----
             uint32_t leaf = 0;
@@ -1213,16 +1211,16 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
             // domain and not strictly inside the void cell (octree cells have disjoint
             // interiors), so the tests before the leaf test (kernel.cu:265, :108) fail.
             const float eps = S.eps();
+            // the hit, horizon and leaf-cell tests as selects, like the start of a step
+            // (configs 2-5: +2-3 % over the branchy form)
             for (uint32_t run = 0;; ++run) {
-                if (sem != 0 && dist < eps) {
-                    finish_ray(a, ray, t, sem, step + 1);
-                    active = false;
-                    break;
-                }
-                t = t + dist;
-                ++step;
-                if (t > a.max_distance || step >= a.max_steps) {
-                    finish_ray(a, ray, t, 0, step);
+                const bool hit = (sem != 0) & (dist < eps);
+                const float tn = t + dist;
+                t = hit ? t : tn;
+                step = hit ? step : step + 1;
+                const bool over = !hit & ((t > a.max_distance) | (step >= a.max_steps));
+                if (hit | over) {
+                    finish_ray(a, ray, t, hit ? sem : 0, hit ? step + 1 : step);
                     active = false;
                     break;
                 }
@@ -1232,9 +1230,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) trace_grid_kernel(const 
                 const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
                 const GridView g = S.grid();
                 // inclusive bounds of the leaf cell: its grid lines (kernel.cu:114)
-                if (!(p.x >= line_at<kShared>(g, 0, cell_lo(lcx)) && p.x <= line_at<kShared>(g, 0, cell_hi(lcx)) &&
-                      p.y >= line_at<kShared>(g, 1, cell_lo(lcy)) && p.y <= line_at<kShared>(g, 1, cell_hi(lcy)) &&
-                      p.z >= line_at<kShared>(g, 2, cell_lo(lcz)) && p.z <= line_at<kShared>(g, 2, cell_hi(lcz))))
+                if (!((p.x >= line_at<kShared>(g, 0, cell_lo(lcx))) & (p.x <= line_at<kShared>(g, 0, cell_hi(lcx))) &
+                      (p.y >= line_at<kShared>(g, 1, cell_lo(lcy))) & (p.y <= line_at<kShared>(g, 1, cell_hi(lcy))) &
+                      (p.z >= line_at<kShared>(g, 2, cell_lo(lcz))) & (p.z <= line_at<kShared>(g, 2, cell_hi(lcz)))))
                     break;
                 dist = leaf_d;
                 sem = leaf_s;
@@ -1394,11 +1392,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
         // memory measured slower on every configuration); option smem_records applies to
         // the float kernel only
         a.n_smem = 0;
-        // five resident blocks for the per-scene launches of scene tables and launches of
-        // 2^21 rays or more (configs 3-5: +3 %), four below (config 2: 5 % faster than five)
-        const bool long_launch = a.seg != nullptr || a.n_rays >= (1u << 21);
-        if constexpr (kMulti) kern = trace_grid_kernel<kFan, kMulti, 3, 4>;
-        else kern = long_launch ? trace_grid_kernel<kFan, kMulti, 3, 5> : trace_grid_kernel<kFan, kMulti, 3, 4>;
+        kern = trace_grid_kernel<kFan, kMulti, 3>;
         base = static_cast<size_t>(kStackLevels + 3) * kThreads * 4u;  // descent stack, reciprocals
         if (!kMulti) base += 3u * static_cast<size_t>(line_row(1 << a.scene.depth)) * 4u;
     } else {
