@@ -8,14 +8,17 @@
 // parameter (0.01 in the reference) and the number of march iterations is an
 // extra output.
 //
-// Execution: a persistent grid (a few blocks per SM).  Each lane owns one ray
-// and runs a small state machine; one loop iteration performs either the start
-// of a march step (position update and cache tests, which often finish the
-// step) or one level of DAG descent (one 4-byte load), then the end of the
-// step if it finished.  Lanes whose ray has ended are refilled at the top of
-// the next iteration from a warp-local range of ray indices; the warp claims
-// ranges of `chunk` rays from a global counter with one atomicAdd, so short
-// rays never leave lanes idle while long rays march on.  Around the trace:
+// Execution: a persistent grid (four blocks of 256 per SM).  Each lane owns one
+// ray and runs a small state machine; one loop iteration performs the start of a
+// march step (position, cell indices and the cache tests, which may finish the
+// step), up to three levels of DAG descent (one 4-byte load each), the exit
+// distance of a void cell, and the end of the step with up to one more step
+// in place inside a cached leaf cell.  Lanes whose ray has ended are refilled,
+// two at a time, at the top of a later iteration from a warp-local range of ray
+// indices; the warp claims ranges of `chunk` rays from a global counter with one
+// atomicAdd, so short rays never leave lanes idle while long rays march on.
+// Decisions that lanes of a warp take differently are written as selects
+// wherever that measured faster than branches.  Around the trace:
 // the claim order of single-scene launches (order_key_kernel,
 // order_scatter_kernel), the scene sort of scene tables (scene_sort_kernel;
 // tables of 2-64 scenes then take one single-scene launch per scene, larger
