@@ -73,7 +73,7 @@ def build_tsdf(force: bool = False, bounds_check: bool = False) -> Path:
     error word, reported by the call) — the stand-in for compute-sanitizer runs."""
     out = LIB / ("libnavi_tsdf_debug.so" if bounds_check else "libnavi_tsdf.so")
     srcs = [CSRC / "tsdf_trace.cu", CSRC / "tsdf_pool.cpp", CSRC / "gmdag_io.cpp"]
-    deps = srcs + [CSRC / "tsdf_internal.h", CSRC / "gmdag_io.h", INCLUDE / "tsdf.h", INCLUDE / "gmdag.h"]
+    deps = srcs + [CSRC / "tsdf_internal.h", CSRC / "exit_quotient.cuh", CSRC / "gmdag_io.h", INCLUDE / "tsdf.h", INCLUDE / "gmdag.h"]
     if force or _stale(out, deps):
         LIB.mkdir(parents=True, exist_ok=True)
         tmp = out.with_suffix(".so.tmp")
@@ -121,14 +121,15 @@ def build_gmdag_gpu(force: bool = False) -> Path:
 
 
 def build_probe(force: bool = False) -> Path:
-    """libnavi_probe.so: the L2 read-bandwidth probe bench.py reports the L2 roofline against."""
+    """libnavi_probe.so: the L2 read-bandwidth probe bench.py reports the L2 roofline against,
+    and the check of the trace kernel's exit quotient against the IEEE division."""
     out = LIB / "libnavi_probe.so"
-    src = CSRC / "peak_probe.cu"
-    if force or _stale(out, [src]):
+    srcs = [CSRC / "peak_probe.cu", CSRC / "quotient_check.cu"]
+    if force or _stale(out, srcs + [CSRC / "exit_quotient.cuh"]):
         LIB.mkdir(parents=True, exist_ok=True)
         tmp = out.with_suffix(".so.tmp")
-        _run([_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", str(src),
-              "-o", str(tmp)])
+        _run([_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+              *map(str, srcs), "-o", str(tmp)])
         tmp.replace(out)
     return out
 

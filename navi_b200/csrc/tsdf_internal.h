@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 #include <mutex>
 #include <string>
@@ -45,7 +46,7 @@ struct HostPool {
 // Per-axis grid lines of the reference's midpoint rule: B[0] = lo, B[2^D] = hi, and for
 // every cell [B[a], B[b]] met by the descent its midpoint B[(a+b)/2] = (B[a] + B[b]) * 0.5f
 // (kernel.cu:166-176); out has 2^D + 2 entries, the last one +inf.  Returns false when the
-// lines are not strictly increasing or the kernel's one-cell estimate bound does not hold.
+// lines are not strictly increasing or the kernel's cell estimate bound does not hold.
 bool build_grid_lines(float lo, float hi, int depth, float* out);
 
 // Record-graph height (hp.height, -1 when cyclic) from record 0.
@@ -91,7 +92,7 @@ struct TsdfSceneDev {
     int32_t depth;                   // grid depth D (cells per axis 2^D); -1: float descent
     float scale[3];                  // 2^D / (bmax - bmin) per axis, float division
     uint32_t n_ext;                  // out-of-line leaves (bounds-checked builds)
-    float offs[3];                   // -(bmin * scale) per axis: cell estimate u = fma(p, scale, offs)
+    float offs[3];                   // fma(-bmin, scale, -0.5) per axis: cell estimate v = fma(p, scale, offs)
 };
 static_assert(sizeof(TsdfSceneDev) == 96, "scene record layout");
 
@@ -107,10 +108,11 @@ struct tsdf_scenes {
 namespace tsdf {
 // Cells per unit length along each axis, 2^D / (bmax - bmin), each an IEEE float
 // subtraction and division (the same values the device's __fsub_rn / __fdiv_rn give),
-// and the offset of the cell estimate u(p) = fma(p, scale, offs), offs = -(bmin * scale)
-// rounded once; build_grid_lines proves the estimate's one-cell bound with the same values.
+// and the offset of the cell estimate v(p) = fma(p, scale, offs), offs = -bmin * scale - 1/2
+// rounded once (half a cell below the cell coordinate); build_grid_lines proves the
+// estimate's bound with the same values.
 inline float grid_scale(float lo, float hi, int depth) { return static_cast<float>(1 << depth) / (hi - lo); }
-inline float grid_offset(float lo, float scale) { return -(lo * scale); }
+inline float grid_offset(float lo, float scale) { return std::fma(-lo, scale, -0.5f); }
 inline void set_grid_scale(TsdfSceneDev& d)
 {
     for (int a = 0; a < 3; ++a) {

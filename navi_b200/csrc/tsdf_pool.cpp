@@ -241,7 +241,7 @@ bool build_grid_lines(float lo, float hi, int depth, float* out)
     const int n = 1 << depth;
     out[0] = lo;
     out[n] = hi;
-    out[n + 1] = std::numeric_limits<float>::infinity();  // padding read by the 3-line lookup
+    out[n + 1] = std::numeric_limits<float>::infinity();  // the +inf sentinel above the top face
     for (int lvl = 0; lvl < depth; ++lvl) {
         const int stride = n >> lvl;
         const int half = stride >> 1;
@@ -249,15 +249,16 @@ bool build_grid_lines(float lo, float hi, int depth, float* out)
     }
     for (int k = 0; k < n; ++k)
         if (!(out[k] < out[k + 1])) return false;
-    // The kernel estimates the cell of p as floor(u(p)), u(p) = RN(p * scale + offs) (one
-    // fused multiply-add) with scale = RN(n / RN(hi - lo)) and offs = -RN(lo * scale), and then
-    // picks among cells e-1, e, e+1.  u is monotone in p (scale > 0), so |u(out[k]) - k| < 1
-    // for every line k bounds the estimate within one cell everywhere.
+    // The kernel estimates the cell of p as e = floor(v(p)), v(p) = RN(p * scale + offs) (one
+    // fused multiply-add) with scale = RN(n / RN(hi - lo)) and offs = RN(-lo * scale - 1/2),
+    // and then picks cell e or e + 1 by the line above e.  v is monotone in p (scale > 0), so
+    // k - 1 <= v(out[k]) < k at every line k puts e at the cell of p or the one below it
+    // everywhere (below the box e <= -1, at or above its top e >= n - 1).
     const float scale = grid_scale(lo, hi, depth);
     const float offs = grid_offset(lo, scale);
     for (int k = 0; k <= n; ++k) {
-        const float u = std::fma(out[k], scale, offs);
-        if (!(std::fabs(u - static_cast<float>(k)) < 1.0f)) return false;
+        const float v = std::fma(out[k], scale, offs);
+        if (!(v >= static_cast<float>(k - 1) && v < static_cast<float>(k))) return false;
     }
     return true;
 }

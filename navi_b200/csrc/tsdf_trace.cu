@@ -35,6 +35,7 @@
 #include <string>
 #include <vector>
 
+#include "exit_quotient.cuh"
 #include "tsdf_internal.h"
 
 namespace {
@@ -685,20 +686,20 @@ __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
 
 // Index of the last grid line <= p: -1 below the box, n at or above its top face (n + 1
 // for p = +inf, which every later test treats as outside), and whether p lies on it.
-// e = floor(u(p)), u(p) = fma(p, scale, offs), clamped to [0, n], is within one cell of
-// the answer (proved per table on the host, build_grid_lines), so three neighbouring lines
-// decide it; the -inf / +inf
-// sentinels at both ends of the row make the box faces need no special case (NaN: -1).
+// v(p) = fma(p, scale, offs), where offs carries a shift of half a cell, is monotone in p
+// with floor(v(B[k])) = k - 1 at every line k (proved per table on the host,
+// build_grid_lines), so e = floor(v(p)), clamped to [-1, n], is the answer or the line
+// below it, and the line above decides.  The -inf / +inf sentinels at both ends of the row
+// make the box faces need no special case; NaN gives e = -1 (fmaxf drops it), the answer -1.
 template <bool kShared>
 __device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float scale, float offs, bool& on)
 {
-    const int e = max(min(__float2int_rz(__fmaf_rn(p, scale, offs)), g.n), 0);
-    const float lm = line_at<kShared>(g, axis, e - 1);
+    const int e = __float2int_rd(fminf(fmaxf(__fmaf_rn(p, scale, offs), -1.0f), static_cast<float>(g.n)));
     const float l0 = line_at<kShared>(g, axis, e);
-    const float lp = line_at<kShared>(g, axis, e + 1);
-    const bool ge0 = p >= l0, gep = p >= lp;
-    on = p == (gep ? lp : (ge0 ? l0 : lm));
-    return e - 1 + (ge0 ? 1 : 0) + (gep ? 1 : 0);
+    const float l1 = line_at<kShared>(g, axis, e + 1);
+    const bool ge1 = p >= l1;
+    on = p == (ge1 ? l1 : l0);
+    return e + (ge1 ? 1 : 0);
 }
 
 // Per-axis reciprocals of a ray's direction, correctly rounded, for the approximate exit
@@ -711,10 +712,11 @@ __device__ __forceinline__ float axis_reciprocal(float dv)
 
 // kernel.cu:54-85 with the void cell's faces read from the grid lines.  Approximate
 // quotients (within 2^-21 relative of the exact ones) pick the axis of the minimum, which
-// alone gets the IEEE division: one division per lane, so a warp whose lanes leave their
-// cells through different faces runs one division sequence, not three.  Axes whose
-// approximate quotient lies within the approximation margin of the minimum (a near tie,
-// rare) get their IEEE division too, so the result is the reference's min over axes.
+// alone gets its correctly rounded quotient, by one fused residual correction of the
+// approximate one (exit_quotient; a warp whose lanes leave their cells through different
+// faces runs one such sequence, not three, and no division).  Axes whose approximate
+// quotient lies within the approximation margin of the minimum (a near tie, rare) get
+// their IEEE division too, so the result is the reference's min over axes.
 // rcp: the lane's per-axis reciprocals of d (ray_reciprocals), NaN on the axes the
 // reference skips (|d| <= 1e-4), whose quotients then drop out of every comparison.
 template <bool kShared>
@@ -730,10 +732,13 @@ __device__ __forceinline__ float cell_exit_distance(const GridView& g, const flo
     // no valid axis, or an infinite / NaN quotient on every valid one: the reference keeps 1000
     if (!(qm < inf)) return kOutside;
     const bool sx = qx == qm, sy = !sx && qy == qm;
-    float t = __fdiv_rn(sx ? ax : (sy ? ay : az), sx ? d.x : (sy ? d.y : d.z));
+    const float as = sx ? ax : (sy ? ay : az), ds = sx ? d.x : (sy ? d.y : d.z);
+    float t = tsdf::exit_quotient(as, ds, sx ? rcp.x : (sy ? rcp.y : rcp.z), qm);
     const float lim = __fmul_rn(qm, 1.0f + 0x1p-19f);
     const bool ox = !sx && qx <= lim, oy = !sy && qy <= lim, oz = (sx || sy) && qz <= lim;
-    if (ox || oy || oz) {  // near tie
+    const bool wide = !(fabsf(ds) < tsdf::kQuotientMaxDivisor);
+    if (ox || oy || oz || wide) {  // near tie, or a divisor outside the correction's range
+        if (wide) t = __fdiv_rn(as, ds);
         if (ox) t = fminf(t, __fdiv_rn(ax, d.x));
         if (oy) t = fminf(t, __fdiv_rn(ay, d.y));
         if (oz) t = fminf(t, __fdiv_rn(az, d.z));

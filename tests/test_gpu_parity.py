@@ -843,3 +843,47 @@ def test_concurrent_callers_on_their_own_streams():
             assert_bits_equal(gd.numpy(), wd.numpy(), f"thread {i} cast {j} dist")
             assert_equal(gs.numpy(), ws.numpy(), f"thread {i} cast {j} sem")
             assert_equal(gk.numpy(), wk.numpy(), f"thread {i} cast {j} steps")
+
+
+def test_non_finite_and_degenerate_rays(descent):
+    """Origins with NaN or +-inf coordinates, origins on the box faces and corners, and
+    directions with every component at or below the 1e-4 threshold of the exit distance
+    (kernel.cu:54-85 then keeps its 1000 m) or exactly zero: the grid descent's sentinel
+    lines and the void exit's no-valid-axis case give the oracle's bits."""
+    cfg = scenes.CONFIGS[1]
+    cs = workloads.compiled_scene(1)
+    lo = np.asarray(cs.bbox_min, np.float32)
+    hi = np.asarray(cs.bbox_max, np.float32)
+    rng = np.random.default_rng(11)
+    origins, dirs = [], []
+    inside = rng.uniform(0.5, 9.5, size=(64, 3)).astype(np.float32)
+    for k, bad in enumerate([np.nan, np.inf, -np.inf]):
+        for axis in range(3):
+            o = inside.copy()
+            o[:, axis] = bad
+            origins.append(o)
+            dirs.append(rng.normal(size=(64, 3)).astype(np.float32))
+    corners = np.array([[x, y, z] for x in (lo[0], hi[0]) for y in (lo[1], hi[1]) for z in (lo[2], hi[2])], np.float32)
+    origins.append(np.repeat(corners, 8, axis=0))
+    dirs.append(rng.normal(size=(64, 3)).astype(np.float32))
+    tiny = rng.choice(np.array([0.0, -0.0, 1e-4, -1e-4, 5e-5, -3e-5], np.float32), size=(64, 3))
+    origins.append(inside)
+    dirs.append(tiny)
+    zero = np.zeros((64, 3), np.float32)
+    zero[::2, 1] = np.float32(1e-4)
+    origins.append(inside)
+    dirs.append(zero)
+    o = np.concatenate(origins).astype(np.float32)
+    v = np.concatenate(dirs).astype(np.float32)
+    norm = np.linalg.norm(v, axis=1, keepdims=True)
+    big = norm[:, 0] > 1e-3
+    v[big] = (v[big] / norm[big]).astype(np.float32)
+    for max_steps, horizon in ((cfg.max_steps, cfg.max_distance), (3, 5000.0)):
+        got_d, got_s, got_k = cast_explicit(cs.words, o, v, max_steps=max_steps, max_distance=horizon,
+                                            bbox_min=cs.bbox_min, bbox_max=cs.bbox_max, hit_epsilon=0.01)
+        ref = O.trace(cs.words, cs.bbox_min, cs.bbox_max, o, v, max_steps=max_steps, max_distance=horizon,
+                      hit_epsilon=0.01)
+        same = (got_d.view(np.uint32) == ref["dist"].view(np.uint32)) | (np.isnan(got_d) & np.isnan(ref["dist"]))
+        assert same.all(), f"dist differs on {np.nonzero(~same)[0][:5]}"
+        assert_equal(got_s, ref["sem"], "sem")
+        assert_equal(got_k, ref["steps"], "steps")
