@@ -625,13 +625,13 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
 // are a fixed set of per-axis grid lines: the root box's faces, and each cell's
 // midpoint (lo + hi) * 0.5f computed once from its two faces.  With D the
 // height of the record graph, the lines B[0..2^D] per axis are built once per
-// block into shared memory.  Each march step converts p to integer cell
-// coordinates (ix = largest k with B[k] <= p, plus "p lies on line ix"), after
-// which every test of the reference is an integer comparison with identical
-// outcome:
-//   p >= mid            <=>  ix >= mid index
-//   closed box test     <=>  lo <= ix && (ix < hi || (ix == hi && on line))
-//   strict box test     <=>  (lo < ix || (lo == ix && !on line)) && ix < hi
+// block into shared memory.  Each march step converts p to doubled integer
+// coordinates (X = 2k on line k, 2k + 1 strictly between lines k and k + 1),
+// after which every test of the reference is an integer comparison with
+// identical outcome:
+//   p >= mid            <=>  X >= 2 x mid index
+//   closed box test     <=>  2 lo <= X <= 2 hi
+//   strict box test     <=>  2 lo < X < 2 hi
 // and a descent only extracts coordinate bits.  The reference starts every
 // descent at the root or at its cached depth-4 node; the path it then follows
 // is a function of the coordinates alone, so the descent here resumes at the
@@ -645,27 +645,18 @@ constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
 constexpr uint32_t kNeedExit = 64u;      // step ended in the void cell: exit distance still to compute
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
 
-// A cell of the finest grid's units: lo | size << 16 (size = 2^shift <= 4096).
-__device__ __forceinline__ uint32_t pack_cell(int j, int shift)
+// Positions on one axis as doubled grid coordinates: X = 2k where p lies on line k
+// (p == B[k]), X = 2k + 1 where it lies strictly between lines k and k + 1.  A cell of the
+// finest grid's units [lo, lo + size] is then one unsigned range test per axis for both
+// of the reference's box tests: the closed box B[lo] <= p <= B[lo + size] is
+// X - 2 lo <u 2 size + 1, its interior B[lo] < p < B[lo + size] is X - (2 lo + 1) <u 2 size - 1.
+// A cached cell keeps the base (2 lo, or 2 lo + 1 for an interior) of each axis and one span
+// (its cells are cubes).
+__device__ __forceinline__ bool in_span(int x, int base, int span)
 {
-    return static_cast<uint32_t>((j >> shift) << shift) | (1u << (shift + 16));
+    return static_cast<uint32_t>(x - base) < static_cast<uint32_t>(span);
 }
-
-__device__ __forceinline__ int cell_lo(uint32_t c) { return static_cast<int>(c & 0xFFFFu); }
-__device__ __forceinline__ int cell_hi(uint32_t c) { return static_cast<int>((c & 0xFFFFu) + (c >> 16)); }
-
-// closed box: lo <= i && (i < hi || (i == hi && on))  <=>  (i - lo) <u size + on
-__device__ __forceinline__ bool cell_closed(uint32_t c, int i, bool on)
-{
-    return static_cast<uint32_t>(i - cell_lo(c)) < (c >> 16) + (on ? 1u : 0u);
-}
-
-// strict box: (lo < i || (lo == i && !on)) && i < hi  <=>  (i - lo - on) <u size - on
-__device__ __forceinline__ bool cell_open(uint32_t c, int i, bool on)
-{
-    const uint32_t o = on ? 1u : 0u;
-    return static_cast<uint32_t>(i - cell_lo(c)) - o < (c >> 16) - o;
-}
+__device__ __forceinline__ int closed_span(int shift) { return (2 << shift) + 1; }
 
 // Per-axis grid lines: rows of line_row(n) = n + 3 floats, -inf, B[0..n], +inf; `lines`
 // points at B[0] of axis 0, so line_at(axis, k) reads B[k] for k in [-1, n + 1].
@@ -684,22 +675,22 @@ __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
     else return __ldg(ptr);
 }
 
-// Index of the last grid line <= p: -1 below the box, n at or above its top face (n + 1
-// for p = +inf, which every later test treats as outside), and whether p lies on it.
-// v(p) = fma(p, scale, offs), where offs carries a shift of half a cell, is monotone in p
-// with floor(v(B[k])) = k - 1 at every line k (proved per table on the host,
-// build_grid_lines), so e = floor(v(p)), clamped to [-1, n], is the answer or the line
-// below it, and the line above decides.  The -inf / +inf sentinels at both ends of the row
-// make the box faces need no special case; NaN gives e = -1 (fmaxf drops it), the answer -1.
+// Doubled grid coordinate of p: 2k + (p on line k ? 0 : 1) for k the last grid line <= p,
+// -1 below the box, n at or above its top face (n + 1 for p = +inf); X <u 2n + 1 is the
+// reference's closed domain test.  v(p) = fma(p, scale, offs), where offs carries a shift of
+// half a cell, is monotone in p with floor(v(B[k])) = k - 1 at every line k (proved per
+// table on the host, build_grid_lines), so e = floor(v(p)), clamped to [-1, n], is k or the
+// line below it, and the line above decides.  The -inf / +inf sentinels at both ends of the
+// row make the box faces need no special case; NaN gives e = -1 (fmaxf drops it), X = -1.
 template <bool kShared>
-__device__ __forceinline__ int grid_index(const GridView& g, int axis, float p, float scale, float offs, bool& on)
+__device__ __forceinline__ int grid_coord(const GridView& g, int axis, float p, float scale, float offs)
 {
     const int e = __float2int_rd(fminf(fmaxf(__fmaf_rn(p, scale, offs), -1.0f), static_cast<float>(g.n)));
     const float l0 = line_at<kShared>(g, axis, e);
     const float l1 = line_at<kShared>(g, axis, e + 1);
     const bool ge1 = p >= l1;
-    on = p == (ge1 ? l1 : l0);
-    return e + (ge1 ? 1 : 0);
+    const bool on = p == (ge1 ? l1 : l0);
+    return 2 * (e + (ge1 ? 1 : 0)) + (on ? 0 : 1);
 }
 
 // Per-axis reciprocals of a ray's direction, correctly rounded, for the approximate exit
@@ -721,12 +712,15 @@ __device__ __forceinline__ float axis_reciprocal(float dv)
 // reference skips (|d| <= 1e-4), whose quotients then drop out of every comparison.
 template <bool kShared>
 __device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
-                                                    const float3 rcp, uint32_t cx, uint32_t cy, uint32_t cz)
+                                                    const float3 rcp, int bx, int by, int bz, int span)
 {
     const float inf = __int_as_float(0x7f800000);
-    const float ax = __fsub_rn(line_at<kShared>(g, 0, d.x > 0.0f ? cell_hi(cx) : cell_lo(cx)), p.x);
-    const float ay = __fsub_rn(line_at<kShared>(g, 1, d.y > 0.0f ? cell_hi(cy) : cell_lo(cy)), p.y);
-    const float az = __fsub_rn(line_at<kShared>(g, 2, d.z > 0.0f ? cell_hi(cz) : cell_lo(cz)), p.z);
+    // the cell's faces from its interior bases 2 lo + 1 and span 2 size - 1
+    const int size = (span + 1) >> 1;
+    const int lx = bx >> 1, ly = by >> 1, lz = bz >> 1;
+    const float ax = __fsub_rn(line_at<kShared>(g, 0, d.x > 0.0f ? lx + size : lx), p.x);
+    const float ay = __fsub_rn(line_at<kShared>(g, 1, d.y > 0.0f ? ly + size : ly), p.y);
+    const float az = __fsub_rn(line_at<kShared>(g, 2, d.z > 0.0f ? lz + size : lz), p.z);
     const float qx = __fmul_rn(ax, rcp.x), qy = __fmul_rn(ay, rcp.y), qz = __fmul_rn(az, rcp.z);
     const float qm = fminf(fminf(qx, qy), qz);
     // no valid axis, or an infinite / NaN quotient on every valid one: the reference keeps 1000
@@ -1030,7 +1024,9 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
     int step = 0;
     uint32_t flags = 0;
     int jx = 0, jy = 0, jz = 0, jpx = 0, jpy = 0, jpz = 0;
-    uint32_t lcx = 0, lcy = 0, lcz = 0, vcx = 0, vcy = 0, vcz = 0, pcx = 0, pcy = 0, pcz = 0;
+    // cached cells as doubled-coordinate bases and spans: leaf (closed), void (interior),
+    // depth-4 prefix (closed; its span follows from the depth)
+    int lbx = 0, lby = 0, lbz = 0, lsp = 0, vbx = 0, vby = 0, vbz = 0, vsp = 0, pbx = 0, pby = 0, pbz = 0;
     float leaf_d = 0.f;
     int32_t leaf_s = 0;
     uint32_t pre_rec = 0, node = 0;
@@ -1071,23 +1067,21 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             const GridView g = S.grid();
             const float3 scale = S.scale(), offs = S.offs();
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
-            bool ex, ey, ez;
-            const int ix = grid_index<kShared>(g, 0, p.x, scale.x, offs.x, ex);
-            const int iy = grid_index<kShared>(g, 1, p.y, scale.y, offs.y, ey);
-            const int iz = grid_index<kShared>(g, 2, p.z, scale.z, offs.z, ez);
+            const int X = grid_coord<kShared>(g, 0, p.x, scale.x, offs.x);
+            const int Y = grid_coord<kShared>(g, 1, p.y, scale.y, offs.y);
+            const int Z = grid_coord<kShared>(g, 2, p.z, scale.z, offs.z);
             // The reference's tests in its order (kernel.cu:265 void cache, :108 domain, :114 leaf
             // cache), all evaluated and combined with selects rather than a chain of branches:
             // lanes of a warp take different outcomes, and the branchy form measured 8 % slower
             // on config 2 and 2.4 % on config 5.  The exit distance of a void-cache hit comes
             // below, with the descents that end in a void cell.
-            const bool hit_void = ((flags & kVoidOk) != 0) & cell_open(vcx, ix, ex) & cell_open(vcy, iy, ey) &
-                                  cell_open(vcz, iz, ez);
-            // closed box test of the domain: 0 <= i < n, or i = n on the top face
-            const bool inside = (static_cast<uint32_t>(ix) < static_cast<uint32_t>(g.n) + (ex ? 1u : 0u)) &
-                                (static_cast<uint32_t>(iy) < static_cast<uint32_t>(g.n) + (ey ? 1u : 0u)) &
-                                (static_cast<uint32_t>(iz) < static_cast<uint32_t>(g.n) + (ez ? 1u : 0u));
-            const bool hit_leaf = ((flags & kLeafOk) != 0) & cell_closed(lcx, ix, ex) & cell_closed(lcy, iy, ey) &
-                                  cell_closed(lcz, iz, ez);
+            const bool hit_void = ((flags & kVoidOk) != 0) & in_span(X, vbx, vsp) & in_span(Y, vby, vsp) &
+                                  in_span(Z, vbz, vsp);
+            // closed box test of the domain: lines 0 to n
+            const int dom = 2 * g.n + 1;
+            const bool inside = in_span(X, 0, dom) & in_span(Y, 0, dom) & in_span(Z, 0, dom);
+            const bool hit_leaf = ((flags & kLeafOk) != 0) & in_span(X, lbx, lsp) & in_span(Y, lby, lsp) &
+                                  in_span(Z, lbz, lsp);
             const bool outside = !hit_void & !inside;
             const bool leaf_hit = !hit_void & inside & hit_leaf;
             flags = hit_void ? (flags | kNeedExit) : flags;
@@ -1095,22 +1089,26 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             sem = outside ? 0 : (leaf_hit ? leaf_s : sem);
             step_done = hit_void | outside | leaf_hit;
             if (!step_done) {
-                const bool use_pre = (flags & kPreOk) && cell_closed(pcx, ix, ex) && cell_closed(pcy, iy, ey) &&
-                                     cell_closed(pcz, iz, ez);
-                // descent coordinates: on the start box's top face the reference keeps taking the upper half
+                const int psh = D - kPrefixDepth;  // prefix cells: 2^psh finest cells a side
+                const int psp = closed_span(max(psh, 0));
+                const bool use_pre = (flags & kPreOk) && in_span(X, pbx, psp) && in_span(Y, pby, psp) &&
+                                     in_span(Z, pbz, psp);
+                // descent coordinates, doubled (2 x the cell index): on the start box's top face
+                // the reference keeps taking the upper half
                 if (use_pre) {
-                    jx = min(ix, cell_hi(pcx) - 1);
-                    jy = min(iy, cell_hi(pcy) - 1);
-                    jz = min(iz, cell_hi(pcz) - 1);
+                    const int top = (2 << psh) - 2;
+                    jx = min(X & ~1, pbx + top);
+                    jy = min(Y & ~1, pby + top);
+                    jz = min(Z & ~1, pbz + top);
                 } else {
-                    jx = min(ix, g.n - 1);
-                    jy = min(iy, g.n - 1);
-                    jz = min(iz, g.n - 1);
+                    jx = min(X & ~1, 2 * g.n - 2);
+                    jy = min(Y & ~1, 2 * g.n - 2);
+                    jz = min(Z & ~1, 2 * g.n - 2);
                 }
                 const int start = use_pre ? kPrefixDepth : 0;
                 const int sd = static_cast<int>((flags >> kSdShift) & 31u);
                 const int sv = (flags & kSvHigh) ? kPrefixDepth : 0;
-                const int common = D - 32 + __clz((jx ^ jpx) | (jy ^ jpy) | (jz ^ jpz));
+                const int common = D - 31 + __clz((jx ^ jpx) | (jy ^ jpy) | (jz ^ jpz));
                 const int reuse = min(common, sd - 1);
                 int level;
                 if (reuse >= start && reuse >= sv) {
@@ -1118,9 +1116,9 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                     node = checked(a.err, level < kStackLevels, kErrStack) ? my_stack[level * kThreads] : S.root();
                     if (!use_pre && level > kPrefixDepth) {
                         pre_rec = my_stack[kPrefixDepth * kThreads];
-                        pcx = pack_cell(jx, D - kPrefixDepth);
-                        pcy = pack_cell(jy, D - kPrefixDepth);
-                        pcz = pack_cell(jz, D - kPrefixDepth);
+                        pbx = jx & (-2 << psh);
+                        pby = jy & (-2 << psh);
+                        pbz = jz & (-2 << psh);
                         flags |= kPreOk;
                     }
                 } else {
@@ -1153,12 +1151,13 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 if (checked(a.err, lvl < kStackLevels, kErrStack)) my_stack[lvl * kThreads] = node;
                 if (lvl == kPrefixDepth && !(flags & kUsePre)) {
                     pre_rec = node;
-                    pcx = pack_cell(jx, D - kPrefixDepth);
-                    pcy = pack_cell(jy, D - kPrefixDepth);
-                    pcz = pack_cell(jz, D - kPrefixDepth);
+                    const int pmask = -2 << (D - kPrefixDepth);
+                    pbx = jx & pmask;
+                    pby = jy & pmask;
+                    pbz = jz & pmask;
                     flags |= kPreOk;
                 }
-                const int sh = D - 1 - lvl;
+                const int sh = D - lvl;  // bit of the level in the doubled coordinates
                 const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
                 uint32_t slot = tsdf::kSlotVoid;
                 if (checked(a.err, node < S.n_recs(), kErrRecord))
@@ -1167,10 +1166,12 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 // A record graph of height D <= 12 ends every path by level D, so the
                 // reference's 32-level cap (kernel.cu:136) is never reached here.
                 if (slot == tsdf::kSlotVoid) {
-                    const uint32_t keep = 0xFFFFu << sh, size = 1u << (sh + 16);  // cells of side 2^sh
-                    vcx = (static_cast<uint32_t>(jx) & keep) | size;
-                    vcy = (static_cast<uint32_t>(jy) & keep) | size;
-                    vcz = (static_cast<uint32_t>(jz) & keep) | size;
+                    // the octant: a cube of 2^(sh - 1) finest cells a side, cached as its interior
+                    const int keep = -1 << sh;
+                    vbx = (jx & keep) | 1;
+                    vby = (jy & keep) | 1;
+                    vbz = (jz & keep) | 1;
+                    vsp = (1 << sh) - 1;
                     flags |= kVoidOk | kNeedExit;
                     done = true;
                 } else if (slot & tsdf::kSlotLeafBit) {
@@ -1182,11 +1183,13 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 }
             }
             if (is_leaf) {
+                // the leaf's cube of 2^sh finest cells a side, cached as a closed box
                 const int sh = D - leaf_level;
-                const uint32_t keep = 0xFFFFu << sh, size = 1u << (sh + 16);
-                lcx = (static_cast<uint32_t>(jx) & keep) | size;
-                lcy = (static_cast<uint32_t>(jy) & keep) | size;
-                lcz = (static_cast<uint32_t>(jz) & keep) | size;
+                const int keep = -2 << sh;
+                lbx = jx & keep;
+                lby = jy & keep;
+                lbz = jz & keep;
+                lsp = (2 << sh) + 1;
                 leaf_d = leaf_distance(leaf);
                 leaf_s = static_cast<int32_t>(leaf >> 16);
                 flags |= kLeafOk;
@@ -1209,7 +1212,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             flags &= ~kNeedExit;
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
             const float3 rcp = make_float3(my_rcp[0], my_rcp[kThreads], my_rcp[2 * kThreads]);
-            dist = cell_exit_distance<kShared>(S.grid(), p, d, rcp, vcx, vcy, vcz);
+            dist = cell_exit_distance<kShared>(S.grid(), p, d, rcp, vbx, vby, vbz, vsp);
             sem = 0;
         }
         if (step_done) {
@@ -1238,9 +1241,10 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
                 const GridView g = S.grid();
                 // inclusive bounds of the leaf cell: its grid lines (kernel.cu:114)
-                if (!((p.x >= line_at<kShared>(g, 0, cell_lo(lcx))) & (p.x <= line_at<kShared>(g, 0, cell_hi(lcx))) &
-                      (p.y >= line_at<kShared>(g, 1, cell_lo(lcy))) & (p.y <= line_at<kShared>(g, 1, cell_hi(lcy))) &
-                      (p.z >= line_at<kShared>(g, 2, cell_lo(lcz))) & (p.z <= line_at<kShared>(g, 2, cell_hi(lcz)))))
+                const int size = lsp >> 1, lx = lbx >> 1, ly = lby >> 1, lz = lbz >> 1;
+                if (!((p.x >= line_at<kShared>(g, 0, lx)) & (p.x <= line_at<kShared>(g, 0, lx + size)) &
+                      (p.y >= line_at<kShared>(g, 1, ly)) & (p.y <= line_at<kShared>(g, 1, ly + size)) &
+                      (p.z >= line_at<kShared>(g, 2, lz)) & (p.z <= line_at<kShared>(g, 2, lz + size))))
                     break;
                 dist = leaf_d;
                 sem = leaf_s;
