@@ -11,7 +11,8 @@
 // Execution: a persistent grid (four blocks of 256 per SM).  Each lane owns one
 // ray and runs a small state machine; one loop iteration performs the start of a
 // march step (position, cell indices and the cache tests, which may finish the
-// step), up to three levels of DAG descent (one 4-byte load each), the exit
+// step), up to three levels of DAG descent (one 4-byte load each), the caching
+// of the cell a descent ended in (once per iteration, not per level), the exit
 // distance of a void cell, and the end of the step with up to one more step
 // in place inside a cached leaf cell.  Lanes whose ray has ended are refilled,
 // two at a time, at the top of a later iteration from a warp-local range of ray
@@ -644,6 +645,7 @@ constexpr int kStackLevels = tsdf::kMaxGridDepth;
 constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
 constexpr uint32_t kNeedExit = 64u;      // step ended in the void cell: exit distance still to compute
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
+constexpr int kFinVoid = 64;             // a descent's end level: ends in an empty octant
 
 // Positions on one axis as doubled grid coordinates: X = 2k where p lies on line k
 // (p == B[k]), X = 2k + 1 where it lies strictly between lines k and k + 1.  A cell of the
@@ -683,14 +685,15 @@ __device__ __forceinline__ float line_at(const GridView& g, int axis, int k)
 // line below it, and the line above decides.  The -inf / +inf sentinels at both ends of the
 // row make the box faces need no special case; NaN gives e = -1 (fmaxf drops it), X = -1.
 template <bool kShared>
-__device__ __forceinline__ int grid_coord(const GridView& g, int axis, float p, float scale, float offs)
+__device__ __forceinline__ int grid_coord(const GridView& g, int axis, float p, float scale, float offs, int& j2)
 {
     const int e = __float2int_rd(fminf(fmaxf(__fmaf_rn(p, scale, offs), -1.0f), static_cast<float>(g.n)));
     const float l0 = line_at<kShared>(g, axis, e);
     const float l1 = line_at<kShared>(g, axis, e + 1);
     const bool ge1 = p >= l1;
     const bool on = p == (ge1 ? l1 : l0);
-    return 2 * (e + (ge1 ? 1 : 0)) + (on ? 0 : 1);
+    j2 = 2 * (e + (ge1 ? 1 : 0));
+    return j2 + (on ? 0 : 1);
 }
 
 // Per-axis reciprocals of a ray's direction, correctly rounded, for the approximate exit
@@ -1067,9 +1070,10 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             const GridView g = S.grid();
             const float3 scale = S.scale(), offs = S.offs();
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
-            const int X = grid_coord<kShared>(g, 0, p.x, scale.x, offs.x);
-            const int Y = grid_coord<kShared>(g, 1, p.y, scale.y, offs.y);
-            const int Z = grid_coord<kShared>(g, 2, p.z, scale.z, offs.z);
+            int X2, Y2, Z2;
+            const int X = grid_coord<kShared>(g, 0, p.x, scale.x, offs.x, X2);
+            const int Y = grid_coord<kShared>(g, 1, p.y, scale.y, offs.y, Y2);
+            const int Z = grid_coord<kShared>(g, 2, p.z, scale.z, offs.z, Z2);
             // The reference's tests in its order (kernel.cu:265 void cache, :108 domain, :114 leaf
             // cache), all evaluated and combined with selects rather than a chain of branches:
             // lanes of a warp take different outcomes, and the branchy form measured 8 % slower
@@ -1097,13 +1101,13 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 // the reference keeps taking the upper half
                 if (use_pre) {
                     const int top = (2 << psh) - 2;
-                    jx = min(X & ~1, pbx + top);
-                    jy = min(Y & ~1, pby + top);
-                    jz = min(Z & ~1, pbz + top);
+                    jx = min(X2, pbx + top);
+                    jy = min(Y2, pby + top);
+                    jz = min(Z2, pbz + top);
                 } else {
-                    jx = min(X & ~1, 2 * g.n - 2);
-                    jy = min(Y & ~1, 2 * g.n - 2);
-                    jz = min(Z & ~1, 2 * g.n - 2);
+                    jx = min(X2, 2 * g.n - 2);
+                    jy = min(Y2, 2 * g.n - 2);
+                    jz = min(Z2, 2 * g.n - 2);
                 }
                 const int start = use_pre ? kPrefixDepth : 0;
                 const int sd = static_cast<int>((flags >> kSdShift) & 31u);
@@ -1131,22 +1135,26 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 lvl = level;
             }
         }
+        // the descent's end, recorded by the level that reaches it and completed once below
+        bool done = false;
+        uint32_t fin = 0;   // the leaf's node word
+        int fin_level = 0;  // level of the cell it ends in, plus kFinVoid for an empty octant
 #pragma unroll
         for (int it = 0; it < kLevels && (flags & kInDesc); ++it) {
             // ---- one descent level (kernel.cu:136-198) ----
-            uint32_t leaf = 0;
-            int leaf_level = lvl;
-            bool is_leaf = false;
-            bool done = false;
             if (node >= tsdf::kSlotExtBit) {
                 // a leaf slot as the descent's start node: the root of a one-leaf DAG
+                uint32_t leaf = 0;
                 if (node & tsdf::kSlotLeafBit) {
                     leaf = node & ~tsdf::kSlotLeafBit;
                 } else if (checked(a.err, (node & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable)) {
                     leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
                                                        (node & tsdf::kSlotIndexMask)));
                 }
-                is_leaf = true;
+                fin = leaf;
+                fin_level = lvl;
+                done = true;
+                flags &= ~kInDesc;
             } else {
                 if (checked(a.err, lvl < kStackLevels, kErrStack)) my_stack[lvl * kThreads] = node;
                 if (lvl == kPrefixDepth && !(flags & kUsePre)) {
@@ -1162,49 +1170,50 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 uint32_t slot = tsdf::kSlotVoid;
                 if (checked(a.err, node < S.n_recs(), kErrRecord))
                     slot = __ldg(S.recs() + (static_cast<size_t>(node) * 8u + oct));
-                leaf_level = lvl + 1;
                 // A record graph of height D <= 12 ends every path by level D, so the
                 // reference's 32-level cap (kernel.cu:136) is never reached here.
-                if (slot == tsdf::kSlotVoid) {
-                    // the octant: a cube of 2^(sh - 1) finest cells a side, cached as its interior
-                    const int keep = -1 << sh;
-                    vbx = (jx & keep) | 1;
-                    vby = (jy & keep) | 1;
-                    vbz = (jz & keep) | 1;
-                    vsp = (1 << sh) - 1;
-                    flags |= kVoidOk | kNeedExit;
+                ++lvl;
+                if (slot == tsdf::kSlotVoid || (slot & tsdf::kSlotLeafBit)) {
+                    fin = slot & ~tsdf::kSlotLeafBit;
+                    fin_level = lvl + (slot == tsdf::kSlotVoid ? kFinVoid : 0);
                     done = true;
-                } else if (slot & tsdf::kSlotLeafBit) {
-                    leaf = slot & ~tsdf::kSlotLeafBit;
-                    is_leaf = true;
+                    flags &= ~kInDesc;
                 } else {
                     node = slot;
-                    lvl = leaf_level;
                 }
             }
-            if (is_leaf) {
-                // the leaf's cube of 2^sh finest cells a side, cached as a closed box
-                const int sh = D - leaf_level;
-                const int keep = -2 << sh;
-                lbx = jx & keep;
-                lby = jy & keep;
-                lbz = jz & keep;
+        }
+        if (done) {
+            // The cell the descent ends in, a cube of 2^sh finest cells a side: an empty octant,
+            // cached as its interior, or a leaf, cached as its closed box (kernel.cu:177-190).
+            const bool vd = fin_level >= kFinVoid;
+            fin_level &= kFinVoid - 1;
+            const int sh = D - fin_level;
+            const int keep = -2 << sh;
+            const int bx = jx & keep, by = jy & keep, bz = jz & keep;
+            if (vd) {
+                vbx = bx | 1;
+                vby = by | 1;
+                vbz = bz | 1;
+                vsp = (2 << sh) - 1;
+                flags |= kVoidOk | kNeedExit;
+            } else {
+                lbx = bx;
+                lby = by;
+                lbz = bz;
                 lsp = (2 << sh) + 1;
-                leaf_d = leaf_distance(leaf);
-                leaf_s = static_cast<int32_t>(leaf >> 16);
+                leaf_d = leaf_distance(fin);
+                leaf_s = static_cast<int32_t>(fin >> 16);
                 flags |= kLeafOk;
                 dist = leaf_d;
                 sem = leaf_s;
-                done = true;
             }
-            if (done) {
-                // records of levels 0..leaf_level-1 now lie on the path of (jx, jy, jz)
-                jpx = jx;
-                jpy = jy;
-                jpz = jz;
-                flags = (flags & ~(kInDesc | (31u << kSdShift))) | (static_cast<uint32_t>(leaf_level) << kSdShift);
-                step_done = true;
-            }
+            // records of levels 0..fin_level-1 now lie on the path of (jx, jy, jz)
+            jpx = jx;
+            jpy = jy;
+            jpz = jz;
+            flags = (flags & ~(31u << kSdShift)) | (static_cast<uint32_t>(fin_level) << kSdShift);
+            step_done = true;
         }
         if (flags & kNeedExit) {
             // the step ended in the void cell (cached or just found): its exit distance,
