@@ -54,12 +54,11 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x)
     return x ^ (x >> 31);
 }
 
-// The kernel's exit distance for one axis: the quotient clamped to [1e-4, 1000], with the
-// IEEE division for divisors of 2^126 and above, and 1000 when the approximate quotient
-// is not finite.
+// The kernel's exit distance for one axis: the quotient, by the IEEE division for divisors
+// of 2^126 and above, capped at 1000 by fminf (which drops a NaN from an overflowed
+// approximate quotient) and floored at 1e-4.
 __device__ __forceinline__ float clamped_exit(float a, float d, float r, float q0)
 {
-    if (!(q0 < __int_as_float(0x7f800000))) return 1000.0f;
     const float t = fabsf(d) < tsdf::kQuotientMaxDivisor ? tsdf::exit_quotient(a, d, r, q0) : __fdiv_rn(a, d);
     return fmaxf(fminf(t, 1000.0f), 1e-4f);
 }

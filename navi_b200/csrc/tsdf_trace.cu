@@ -644,8 +644,8 @@ __global__ void __launch_bounds__(kThreads) trace_float_kernel(const TraceArgs a
 constexpr int kStackLevels = tsdf::kMaxGridDepth;
 constexpr uint32_t kSvHigh = 32u;        // stack levels 0..3 not valid
 constexpr uint32_t kNeedExit = 64u;      // step ended in the void cell: exit distance still to compute
+constexpr uint32_t kWideRay = 128u;      // a direction component of magnitude 2^126 or more
 constexpr int kSdShift = 8;              // 5 bits: number of valid stack levels
-constexpr int kFinVoid = 64;             // a descent's end level: ends in an empty octant
 
 // Positions on one axis as doubled grid coordinates: X = 2k where p lies on line k
 // (p == B[k]), X = 2k + 1 where it lies strictly between lines k and k + 1.  A cell of the
@@ -704,43 +704,35 @@ __device__ __forceinline__ float axis_reciprocal(float dv)
     return fabsf(dv) > kDirEps ? __frcp_rn(dv) : __int_as_float(0x7fc00000);
 }
 
-// kernel.cu:54-85 with the void cell's faces read from the grid lines.  Approximate
-// quotients (within 2^-21 relative of the exact ones) pick the axis of the minimum, which
-// alone gets its correctly rounded quotient, by one fused residual correction of the
-// approximate one (exit_quotient; a warp whose lanes leave their cells through different
-// faces runs one such sequence, not three, and no division).  Axes whose approximate
-// quotient lies within the approximation margin of the minimum (a near tie, rare) get
-// their IEEE division too, so the result is the reference's min over axes.
-// rcp: the lane's per-axis reciprocals of d (ray_reciprocals), NaN on the axes the
-// reference skips (|d| <= 1e-4), whose quotients then drop out of every comparison.
+// kernel.cu:54-85 with the void cell's faces read from the grid lines: the minimum over
+// the axes of the IEEE quotients (face - p) / d, each from the lane's reciprocal of d by
+// exit_quotient (no division), capped at 1000 and floored at 1e-4.  rcp: the lane's
+// per-axis reciprocals of d, NaN on the axes the reference skips (|d| <= 1e-4), whose
+// quotients are then NaN and drop out of fminf.  wide: a component of d is 2^126 or more
+// in magnitude, where exit_quotient does not apply; such rays divide.  The quotients are
+// never negative: p lies in the closed cell and each face is the one d points to.
 template <bool kShared>
 __device__ __forceinline__ float cell_exit_distance(const GridView& g, const float3 p, const float3 d,
-                                                    const float3 rcp, int bx, int by, int bz, int span)
+                                                    const float3 rcp, int bx, int by, int bz, int span, bool wide)
 {
-    const float inf = __int_as_float(0x7f800000);
     // the cell's faces from its interior bases 2 lo + 1 and span 2 size - 1
     const int size = (span + 1) >> 1;
     const int lx = bx >> 1, ly = by >> 1, lz = bz >> 1;
     const float ax = __fsub_rn(line_at<kShared>(g, 0, d.x > 0.0f ? lx + size : lx), p.x);
     const float ay = __fsub_rn(line_at<kShared>(g, 1, d.y > 0.0f ? ly + size : ly), p.y);
     const float az = __fsub_rn(line_at<kShared>(g, 2, d.z > 0.0f ? lz + size : lz), p.z);
-    const float qx = __fmul_rn(ax, rcp.x), qy = __fmul_rn(ay, rcp.y), qz = __fmul_rn(az, rcp.z);
-    const float qm = fminf(fminf(qx, qy), qz);
-    // no valid axis, or an infinite / NaN quotient on every valid one: the reference keeps 1000
-    if (!(qm < inf)) return kOutside;
-    const bool sx = qx == qm, sy = !sx && qy == qm;
-    const float as = sx ? ax : (sy ? ay : az), ds = sx ? d.x : (sy ? d.y : d.z);
-    float t = tsdf::exit_quotient(as, ds, sx ? rcp.x : (sy ? rcp.y : rcp.z), qm);
-    const float lim = __fmul_rn(qm, 1.0f + 0x1p-19f);
-    const bool ox = !sx && qx <= lim, oy = !sy && qy <= lim, oz = (sx || sy) && qz <= lim;
-    const bool wide = !(fabsf(ds) < tsdf::kQuotientMaxDivisor);
-    if (ox || oy || oz || wide) {  // near tie, or a divisor outside the correction's range
-        if (wide) t = __fdiv_rn(as, ds);
-        if (ox) t = fminf(t, __fdiv_rn(ax, d.x));
-        if (oy) t = fminf(t, __fdiv_rn(ay, d.y));
-        if (oz) t = fminf(t, __fdiv_rn(az, d.z));
+    float tx, ty, tz;
+    if (!wide) {
+        tx = tsdf::exit_quotient(ax, d.x, rcp.x, __fmul_rn(ax, rcp.x));
+        ty = tsdf::exit_quotient(ay, d.y, rcp.y, __fmul_rn(ay, rcp.y));
+        tz = tsdf::exit_quotient(az, d.z, rcp.z, __fmul_rn(az, rcp.z));
+    } else {
+        const float nan = __int_as_float(0x7fc00000);
+        tx = rcp.x == rcp.x ? __fdiv_rn(ax, d.x) : nan;
+        ty = rcp.y == rcp.y ? __fdiv_rn(ay, d.y) : nan;
+        tz = rcp.z == rcp.z ? __fdiv_rn(az, d.z) : nan;
     }
-    return fmaxf(fminf(t, kOutside), kVoidAdvance);
+    return fmaxf(fminf(fminf(fminf(tx, ty), tz), kOutside), kVoidAdvance);
 }
 
 // Claim rays for the idle lanes of the warp: returns this lane's new ray or ~0u.  A
@@ -1049,7 +1041,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             dist = 0.f;
             sem = 0;
             step = 0;
-            flags = 0;
+            flags = fmaxf(fmaxf(fabsf(d.x), fabsf(d.y)), fabsf(d.z)) < tsdf::kQuotientMaxDivisor ? 0u : kWideRay;
             if constexpr (kMulti) {
                 if (static_cast<uint32_t>(scene) >= a.n_scenes) {
                     // no such scene: the ray is not traced (NaN distance, semantic 0, 0 steps)
@@ -1065,6 +1057,10 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
 
         const int D = S.depth();
         bool step_done = false;
+        // the descent's end, recorded where it is reached and completed once below
+        bool done = false;
+        uint32_t fin = 0;   // the slot it ends in: tsdf::kSlotVoid or a leaf slot
+        int fin_level = 0;  // level of that cell
         if (!(flags & kInDesc)) {
             // ---- start of a march step (kernel.cu:260-294) ----
             const GridView g = S.grid();
@@ -1114,80 +1110,49 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 const int sv = (flags & kSvHigh) ? kPrefixDepth : 0;
                 const int common = D - 31 + __clz((jx ^ jpx) | (jy ^ jpy) | (jz ^ jpz));
                 const int reuse = min(common, sd - 1);
-                int level;
-                if (reuse >= start && reuse >= sv) {
-                    level = reuse;
-                    node = checked(a.err, level < kStackLevels, kErrStack) ? my_stack[level * kThreads] : S.root();
-                    if (!use_pre && level > kPrefixDepth) {
-                        pre_rec = my_stack[kPrefixDepth * kThreads];
-                        pbx = jx & (-2 << psh);
-                        pby = jy & (-2 << psh);
-                        pbz = jz & (-2 << psh);
-                        flags |= kPreOk;
-                    }
-                } else {
-                    level = start;
-                    node = use_pre ? pre_rec : S.root();
-                    if (use_pre) flags |= kSvHigh;
-                    else flags &= ~kSvHigh;
-                }
+                // resume at the deepest valid stack level on the path, else at the start node
+                const bool resume = (reuse >= start) & (reuse >= sv);
+                const int level = resume ? reuse : start;
+                const uint32_t kept =  // level <= D - 1 < kStackLevels
+                    checked(a.err, level < kStackLevels, kErrStack) ? my_stack[level * kThreads] : S.root();
+                node = resume ? kept : (use_pre ? pre_rec : S.root());
+                flags = resume ? flags : (use_pre ? (flags | kSvHigh) : (flags & ~kSvHigh));
                 flags = (flags & ~kUsePre) | kInDesc | (use_pre ? kUsePre : 0u);
                 lvl = level;
+                if (node >= tsdf::kSlotExtBit) {
+                    // the root slot of a one-leaf DAG (stack and prefix entries are records)
+                    fin = node;
+                    fin_level = 0;
+                    done = true;
+                }
             }
         }
-        // the descent's end, recorded by the level that reaches it and completed once below
-        bool done = false;
-        uint32_t fin = 0;   // the leaf's node word
-        int fin_level = 0;  // level of the cell it ends in, plus kFinVoid for an empty octant
+        bool descend = (flags & kInDesc) && !done;
 #pragma unroll
-        for (int it = 0; it < kLevels && (flags & kInDesc); ++it) {
+        for (int it = 0; it < kLevels && descend; ++it) {
             // ---- one descent level (kernel.cu:136-198) ----
-            if (node >= tsdf::kSlotExtBit) {
-                // a leaf slot as the descent's start node: the root of a one-leaf DAG
-                uint32_t leaf = 0;
-                if (node & tsdf::kSlotLeafBit) {
-                    leaf = node & ~tsdf::kSlotLeafBit;
-                } else if (checked(a.err, (node & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable)) {
-                    leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
-                                                       (node & tsdf::kSlotIndexMask)));
-                }
-                fin = leaf;
+            if (checked(a.err, lvl < kStackLevels, kErrStack)) my_stack[lvl * kThreads] = node;
+            const int sh = D - lvl;  // bit of the level in the doubled coordinates
+            const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
+            uint32_t slot = tsdf::kSlotVoid;
+            if (checked(a.err, node < S.n_recs(), kErrRecord))
+                slot = __ldg(S.recs() + (static_cast<size_t>(node) * 8u + oct));
+            // A record graph of height D <= 12 ends every path by level D, so the
+            // reference's 32-level cap (kernel.cu:136) is never reached here.
+            ++lvl;
+            if (slot >= tsdf::kSlotExtBit) {  // an empty octant or a leaf
+                fin = slot;
                 fin_level = lvl;
                 done = true;
-                flags &= ~kInDesc;
+                descend = false;
             } else {
-                if (checked(a.err, lvl < kStackLevels, kErrStack)) my_stack[lvl * kThreads] = node;
-                if (lvl == kPrefixDepth && !(flags & kUsePre)) {
-                    pre_rec = node;
-                    const int pmask = -2 << (D - kPrefixDepth);
-                    pbx = jx & pmask;
-                    pby = jy & pmask;
-                    pbz = jz & pmask;
-                    flags |= kPreOk;
-                }
-                const int sh = D - lvl;  // bit of the level in the doubled coordinates
-                const uint32_t oct = ((jx >> sh) & 1) | (((jy >> sh) & 1) << 1) | (((jz >> sh) & 1) << 2);
-                uint32_t slot = tsdf::kSlotVoid;
-                if (checked(a.err, node < S.n_recs(), kErrRecord))
-                    slot = __ldg(S.recs() + (static_cast<size_t>(node) * 8u + oct));
-                // A record graph of height D <= 12 ends every path by level D, so the
-                // reference's 32-level cap (kernel.cu:136) is never reached here.
-                ++lvl;
-                if (slot == tsdf::kSlotVoid || (slot & tsdf::kSlotLeafBit)) {
-                    fin = slot & ~tsdf::kSlotLeafBit;
-                    fin_level = lvl + (slot == tsdf::kSlotVoid ? kFinVoid : 0);
-                    done = true;
-                    flags &= ~kInDesc;
-                } else {
-                    node = slot;
-                }
+                node = slot;
             }
         }
         if (done) {
             // The cell the descent ends in, a cube of 2^sh finest cells a side: an empty octant,
             // cached as its interior, or a leaf, cached as its closed box (kernel.cu:177-190).
-            const bool vd = fin_level >= kFinVoid;
-            fin_level &= kFinVoid - 1;
+            const bool vd = fin == tsdf::kSlotVoid;
             const int sh = D - fin_level;
             const int keep = -2 << sh;
             const int bx = jx & keep, by = jy & keep, bz = jz & keep;
@@ -1202,17 +1167,35 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 lby = by;
                 lbz = bz;
                 lsp = (2 << sh) + 1;
-                leaf_d = leaf_distance(fin);
-                leaf_s = static_cast<int32_t>(fin >> 16);
+                uint32_t leaf = fin & ~tsdf::kSlotLeafBit;
+                if (!(fin & tsdf::kSlotLeafBit)) {
+                    // a leaf stored out of line (semantic >= 0x7FFF)
+                    leaf = 0;
+                    if (checked(a.err, (fin & tsdf::kSlotIndexMask) < S.n_ext(), kErrLeafTable))
+                        leaf = static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned long long*>(S.ext()) +
+                                                           (fin & tsdf::kSlotIndexMask)));
+                }
+                leaf_d = leaf_distance(leaf);
+                leaf_s = static_cast<int32_t>(leaf >> 16);
                 flags |= kLeafOk;
                 dist = leaf_d;
                 sem = leaf_s;
+            }
+            // The reference caches the depth-4 node of a descent that did not start there
+            // (kernel.cu:154-163): the record at level 4 of this path, from the stack.
+            if (!(flags & kUsePre) && fin_level > kPrefixDepth) {
+                pre_rec = my_stack[kPrefixDepth * kThreads];
+                const int pmask = -2 << (D - kPrefixDepth);
+                pbx = jx & pmask;
+                pby = jy & pmask;
+                pbz = jz & pmask;
+                flags |= kPreOk;
             }
             // records of levels 0..fin_level-1 now lie on the path of (jx, jy, jz)
             jpx = jx;
             jpy = jy;
             jpz = jz;
-            flags = (flags & ~(31u << kSdShift)) | (static_cast<uint32_t>(fin_level) << kSdShift);
+            flags = (flags & ~(kInDesc | (31u << kSdShift))) | (static_cast<uint32_t>(fin_level) << kSdShift);
             step_done = true;
         }
         if (flags & kNeedExit) {
@@ -1221,7 +1204,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             flags &= ~kNeedExit;
             const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
             const float3 rcp = make_float3(my_rcp[0], my_rcp[kThreads], my_rcp[2 * kThreads]);
-            dist = cell_exit_distance<kShared>(S.grid(), p, d, rcp, vbx, vby, vbz, vsp);
+            dist = cell_exit_distance<kShared>(S.grid(), p, d, rcp, vbx, vby, vbz, vsp, (flags & kWideRay) != 0);
             sem = 0;
         }
         if (step_done) {

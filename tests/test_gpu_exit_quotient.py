@@ -1,11 +1,11 @@
 """The trace kernel's exit quotient (navi_b200/csrc/exit_quotient.cuh) against the IEEE
 division __fdiv_rn on the device, bit for bit.
 
-The grid kernel divides once per void exit by one fused residual correction of
-RN(a * RN(1 / d)) instead of a division.  These tests check that identity over slices of
-the binary32 significand pairs (exhaustively over all 2^46 pairs with
-NAVI_QUOTIENT_EXHAUSTIVE=1, about a minute on one B200) and over sampled exponents and
-signs, through navi_b200/csrc/quotient_check.cu in libnavi_probe.so.
+The grid kernel computes each quotient of a void cell's exit distance by one fused
+residual correction of RN(a * RN(1 / d)) instead of a division.  These tests check that
+identity over slices of the binary32 significand pairs (exhaustively over all 2^46 pairs
+with NAVI_QUOTIENT_EXHAUSTIVE=1, about a minute on one B200) and over sampled exponents
+and signs, through navi_b200/csrc/quotient_check.cu in libnavi_probe.so.
 """
 
 from __future__ import annotations
