@@ -1057,6 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
 
         const int D = S.depth();
         bool step_done = false;
+        bool leaf_step = false;  // the step ends in the cached leaf cell
         // the descent's end, recorded where it is reached and completed once below
         bool done = false;
         uint32_t fin = 0;   // the slot it ends in: tsdf::kSlotVoid or a leaf slot
@@ -1088,6 +1089,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             dist = outside ? kOutside : (leaf_hit ? leaf_d : dist);
             sem = outside ? 0 : (leaf_hit ? leaf_s : sem);
             step_done = hit_void | outside | leaf_hit;
+            leaf_step = leaf_hit;
             if (!step_done) {
                 const int psh = D - kPrefixDepth;  // prefix cells: 2^psh finest cells a side
                 const int psp = closed_span(max(psh, 0));
@@ -1156,17 +1158,16 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             const int sh = D - fin_level;
             const int keep = -2 << sh;
             const int bx = jx & keep, by = jy & keep, bz = jz & keep;
-            if (vd) {
-                vbx = bx | 1;
-                vby = by | 1;
-                vbz = bz | 1;
-                vsp = (2 << sh) - 1;
-                flags |= kVoidOk | kNeedExit;
-            } else {
-                lbx = bx;
-                lby = by;
-                lbz = bz;
-                lsp = (2 << sh) + 1;
+            vbx = vd ? (bx | 1) : vbx;
+            vby = vd ? (by | 1) : vby;
+            vbz = vd ? (bz | 1) : vbz;
+            vsp = vd ? (2 << sh) - 1 : vsp;
+            lbx = vd ? lbx : bx;
+            lby = vd ? lby : by;
+            lbz = vd ? lbz : bz;
+            lsp = vd ? lsp : (2 << sh) + 1;
+            flags |= vd ? (kVoidOk | kNeedExit) : 0u;
+            if (!vd) {
                 uint32_t leaf = fin & ~tsdf::kSlotLeafBit;
                 if (!(fin & tsdf::kSlotLeafBit)) {
                     // a leaf stored out of line (semantic >= 0x7FFF)
@@ -1178,6 +1179,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 leaf_d = leaf_distance(leaf);
                 leaf_s = static_cast<int32_t>(leaf >> 16);
                 flags |= kLeafOk;
+                leaf_step = true;
                 dist = leaf_d;
                 sem = leaf_s;
             }
@@ -1208,11 +1210,12 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
             sem = 0;
         }
         if (step_done) {
-            // ---- end of the march step (kernel.cu:297-304), then up to leaf_run more steps in
-            // place while the next position stays in the cached leaf cell.  Such a step is a
-            // leaf-cache hit in the reference: a point of the closed leaf box is inside the
-            // domain and not strictly inside the void cell (octree cells have disjoint
-            // interiors), so the tests before the leaf test (kernel.cu:265, :108) fail.
+            // ---- end of the march step (kernel.cu:297-304), then, after a step that ended in
+            // the cached leaf cell, up to leaf_run more steps in place while the next position
+            // stays in that cell.  Such a step is a leaf-cache hit in the reference: a point of
+            // the closed leaf box is inside the domain and not strictly inside the void cell
+            // (octree cells have disjoint interiors), so the tests before the leaf test
+            // (kernel.cu:265, :108) fail.
             const float eps = S.eps();
             // the hit, horizon and leaf-cell tests as selects, like the start of a step
             // (configs 2-5: +2-3 % over the branchy form)
@@ -1229,7 +1232,7 @@ __global__ void __launch_bounds__(kThreads, 4) trace_grid_kernel(const TraceArgs
                 }
                 // multi-scene launches read the lines from global memory, where the run
                 // costs more than it saves (config 3: -9%); single-scene launches only
-                if (kMulti || run >= a.leaf_run || !(flags & kLeafOk)) break;
+                if (kMulti || run >= a.leaf_run || !leaf_step) break;
                 const float3 p = make_float3(__fmaf_rn(t, d.x, o.x), __fmaf_rn(t, d.y, o.y), __fmaf_rn(t, d.z, o.z));
                 const GridView g = S.grid();
                 // inclusive bounds of the leaf cell: its grid lines (kernel.cu:114)
