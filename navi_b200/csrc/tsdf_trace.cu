@@ -11,7 +11,7 @@
 // Execution: a persistent grid (four blocks of 256 per SM).  Each lane owns one
 // ray and runs a small state machine; one loop iteration performs the start of a
 // march step (position, cell indices and the cache tests, which may finish the
-// step), up to three levels of DAG descent (one 4-byte load each), the caching
+// step), up to four levels of DAG descent (one 4-byte load each), the caching
 // of the cell a descent ended in (once per iteration, not per level), the exit
 // distance of a void cell, and the end of the step with up to one more step
 // in place inside a cached leaf cell.  Lanes whose ray has ended are refilled,
@@ -1399,7 +1399,7 @@ int launch(Kind kind, TraceArgs& a, int device, void* workspace, cudaStream_t st
         // memory measured slower on every configuration); option smem_records applies to
         // the float kernel only
         a.n_smem = 0;
-        kern = trace_grid_kernel<kFan, kMulti, 3>;
+        kern = trace_grid_kernel<kFan, kMulti, 4>;
         base = static_cast<size_t>(kStackLevels + 3) * kThreads * 4u;  // descent stack, reciprocals
         if (!kMulti) base += 3u * static_cast<size_t>(line_row(1 << a.scene.depth)) * 4u;
     } else {
