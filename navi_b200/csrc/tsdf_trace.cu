@@ -696,9 +696,9 @@ __device__ __forceinline__ int grid_coord(const GridView& g, int axis, float p, 
     return j2 + (on ? 0 : 1);
 }
 
-// Per-axis reciprocals of a ray's direction, correctly rounded, for the approximate exit
-// quotients (a * RN(1/d) is within 2^-22 relative of a / d); NaN where |d| <= 1e-4, the
-// axes kernel.cu:54-85 leaves out.  Kept per lane in shared memory while the ray lives.
+// Per-axis reciprocals of a ray's direction, correctly rounded, from which exit_quotient
+// computes the exit quotients; NaN where |d| <= 1e-4, the axes kernel.cu:54-85 leaves out.
+// Kept per lane in shared memory while the ray lives.
 __device__ __forceinline__ float axis_reciprocal(float dv)
 {
     return fabsf(dv) > kDirEps ? __frcp_rn(dv) : __int_as_float(0x7fc00000);
